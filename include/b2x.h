@@ -1,0 +1,207 @@
+/*
+ * b2x — C ABI of the B200-native fp8 GEMM / fp8 cast / split-K library.
+ *
+ * This is the drop-in boundary that replaces, for one data path, what the
+ * reference reaches through Triton plugin machinery:
+ *   - the op-level Python entry point `matmul(a, b, config=None, use_heuristic=False)`
+ *     (extensions/utlx/tlx/tutorials/blackwell_gemm_ws.py:1352) and the kernel
+ *     it launches, `matmul_kernel_tma_ws_blackwell` (:1089-1349);
+ *   - the split-K reduction `_reduce_k_kernel` (blackwell_gemm_ws.py:1033-1056);
+ *   - the fp8 quantize helper `_compute_scale_and_quantize`
+ *     (extensions/utlx/tlx/language/tlx/mxfp8_utils.py:13-86) and the
+ *     fp32 -> fp8 cast it ends in (`.to(fp8)`, round-to-nearest-even).
+ * The reference's own binary boundary, `tritonGetPluginInfo()`
+ * (extensions/utlx/uTLXPlugin.cpp:700-814), is compile-time MLIR plumbing and
+ * has no counterpart here: b2x ships finished sm_100a kernels.
+ *
+ * Conventions
+ *   - Plain pointers and sizes; no torch types.  All device pointers belong to
+ *     the caller, including workspaces (query their size first).
+ *   - Every call is asynchronous on the given stream (cudaStream_t passed as
+ *     void*; NULL = legacy default stream) and never synchronises.
+ *   - No C++ exception crosses this ABI.  Errors come back as a b2x_status;
+ *     b2x_last_error() gives a message for the calling thread's last failure.
+ *   - Thread-safe: the only shared state is a per-device cache of kernel
+ *     attributes guarded by a mutex.
+ *   - Kernels never trap.  Every internal wait is bounded; a wait that gives
+ *     up records a code in a per-device status word (b2x_read_device_status)
+ *     and the kernel returns early.
+ */
+#ifndef B2X_H_
+#define B2X_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define B2X_ABI_VERSION 1
+
+#if defined(__GNUC__)
+#define B2X_API __attribute__((visibility("default")))
+#else
+#define B2X_API
+#endif
+
+typedef enum {
+  B2X_OK = 0,
+  B2X_ERR_INVALID_ARG = 1,  /* bad shape / stride / pointer / alignment */
+  B2X_ERR_UNSUPPORTED = 2,  /* valid request this build does not implement */
+  B2X_ERR_CUDA = 3,         /* a CUDA runtime/driver call failed */
+  B2X_ERR_TIMEOUT = 4,      /* a kernel wait gave up (see b2x_read_device_status) */
+  B2X_ERR_WORKSPACE = 5     /* workspace missing or too small */
+} b2x_status;
+
+typedef enum {
+  B2X_F32 = 0,
+  B2X_BF16 = 1,
+  B2X_F16 = 2,
+  B2X_E4M3 = 3, /* float8_e4m3fn: bias 7, max 448, no inf, NaN = S.1111.111 */
+  B2X_E5M2 = 4, /* float8_e5m2: bias 15, max 57344, IEEE-style inf/NaN */
+  B2X_U8 = 5    /* raw bytes, used for E8M0 scales */
+} b2x_dtype;
+
+/* How an fp8 tensor is scaled: x ~= q * scale. */
+typedef enum {
+  B2X_SCALE_NONE = 0,         /* scale = 1, plain saturating RNE cast */
+  B2X_SCALE_TENSOR = 1,       /* one fp32 scale for the tensor, computed from amax */
+  B2X_SCALE_TENSOR_GIVEN = 2, /* one fp32 scale supplied by the caller (static) */
+  B2X_SCALE_BLOCK_1x128 = 3,  /* fp32 scale per (row, 128-column block) */
+  B2X_SCALE_BLOCK_128x128 = 4,/* fp32 scale per (128-row, 128-column) tile */
+  B2X_SCALE_MX_1x32 = 5       /* E8M0 (uint8 biased exponent) per (row, 32-column block), RCEIL */
+} b2x_scale_mode;
+
+/* ------------------------------------------------------------------ cast */
+
+/*
+ * Quantize a 2-D fp32/bf16 tensor x[rows, cols] (row stride ld_x elements,
+ * unit column stride) to fp8 q[rows, cols] (row stride ld_q), computing (or,
+ * for B2X_SCALE_TENSOR_GIVEN, reading) the scales.
+ *
+ * Per group of elements sharing one scale (amax is a NaN-ignoring max of |x|):
+ *   scale = amax / FMAX                    (IEEE fp32 division; FMAX 448 / 57344)
+ *   inv   = scale == 0 ? 0 : 1 / scale     (IEEE fp32 division)
+ *   q     = fp8_rne_satfinite(clamp(x * inv, -FMAX, FMAX))
+ * and for B2X_SCALE_MX_1x32 the scale is rounded up to a power of two (RCEIL)
+ * and stored as its biased exponent byte.
+ * Replaces: _compute_scale_and_quantize, mxfp8_utils.py:13-86 (1x32 E8M0) and
+ * the per-tensor / 1x128 / 128x128 amax scaling of the same recipe.
+ *
+ * scale layout (row-major, ld_scale elements per row):
+ *   TENSOR / TENSOR_GIVEN: 1 fp32
+ *   BLOCK_1x128:           [rows, ceil(cols/128)] fp32
+ *   BLOCK_128x128:         [ceil(rows/128), ceil(cols/128)] fp32
+ *   MX_1x32:               [rows, ceil(cols/32)] uint8
+ */
+typedef struct {
+  const void* x;
+  b2x_dtype x_type; /* B2X_F32 or B2X_BF16 */
+  int64_t rows, cols, ld_x;
+  void* q;
+  b2x_dtype q_type; /* B2X_E4M3 or B2X_E5M2 */
+  int64_t ld_q;
+  void* scale;
+  b2x_scale_mode mode;
+  int64_t ld_scale;
+  void* workspace; /* B2X_SCALE_TENSOR only: see b2x_cast_workspace_size */
+  size_t workspace_bytes;
+} b2x_cast_args;
+
+B2X_API size_t b2x_cast_workspace_size(const b2x_cast_args* args);
+B2X_API b2x_status b2x_fp8_cast(const b2x_cast_args* args, void* stream);
+
+/* Amax only (NaN-ignoring max |x|) of a 2-D tensor, written as one fp32. */
+B2X_API b2x_status b2x_amax(const void* x, b2x_dtype x_type, int64_t rows, int64_t cols, int64_t ld_x, float* amax_out,
+                    void* workspace, size_t workspace_bytes, void* stream);
+
+/* ------------------------------------------------------------------ GEMM */
+
+/*
+ * Tile / pipeline configuration.  Same keys as the reference's config dict
+ * (blackwell_gemm_ws.py:1097-1109); zero means "pick".  NUM_MMA_GROUPS,
+ * NUM_CTAS and INTERLEAVE_EPILOGUE are accepted for drop-in compatibility:
+ * this build's CTA tile is always one 128-row tcgen05 MMA group on one SM.
+ */
+typedef struct {
+  int block_m, block_n, block_k;
+  int group_size_m;
+  int num_smem_buffers, num_tmem_buffers;
+  int num_mma_groups, epilogue_subtile;
+  int num_ctas, split_k, interleave_epilogue;
+} b2x_gemm_config;
+
+/*
+ * C[M,N] = out_cast( sum_k A[m,k] * B[k,n] * scales )
+ *   A: fp8 [M,K], row stride lda (elements), K contiguous.
+ *   B: fp8, logical [K,N] as in the reference (b.shape == (K, N)); strides
+ *      (ldb_k, ldb_n) with exactly one of them equal to 1:
+ *        ldb_k == 1  -> B stored "K-major" (an nn.Linear weight [N,K] viewed as w.t())
+ *        ldb_n == 1  -> B stored row-major [K,N]
+ *   C: bf16 / fp16 / fp32 [M,N], row stride ldc.
+ * Scales (fp32, device pointers):
+ *   B2X_SCALE_NONE:   none;
+ *   B2X_SCALE_TENSOR / _GIVEN: scale_a[0], scale_b[0]   -> C = sA*sB*(A.B)
+ *   B2X_SCALE_BLOCK_1x128 (A) with 128x128 (B): scale_a[m, kb] at
+ *      scale_a + m*sa_stride_m + kb*sa_stride_k, scale_b[kb, nb] at
+ *      scale_b + kb*sb_stride_k + nb*sb_stride_n; promotion per 128-deep
+ *      K block: C = sum_kb sA[m,kb]*sB[kb,nb]*(A_kb.B_kb).
+ * Split-K (config.split_k > 1): fp32 partials are reduced with
+ * red.global.add.v4.f32 into a workspace; the last CTA to finish a tile
+ * writes C.  The workspace must be all zero on the first call and is left all
+ * zero by every successful call (so it can be cached and reused on one
+ * stream); see b2x_gemm_workspace_size.
+ * Replaces: matmul(a, b, config, use_heuristic) blackwell_gemm_ws.py:1352-1483
+ * together with its kernel (:1089-1349) and split-K reduce (:1033-1079).
+ */
+typedef struct {
+  const void* a;
+  const void* b;
+  void* c;
+  int64_t M, N, K;
+  int64_t lda;
+  int64_t ldb_k, ldb_n;
+  int64_t ldc;
+  b2x_dtype a_type, b_type, c_type;
+  b2x_scale_mode scale_mode;
+  const float* scale_a;
+  int64_t sa_stride_m, sa_stride_k;
+  const float* scale_b;
+  int64_t sb_stride_k, sb_stride_n;
+  void* workspace;
+  size_t workspace_bytes;
+  b2x_gemm_config config;
+} b2x_gemm_args;
+
+/* Fill in a config for the shape (the counterpart of get_heuristic_config,
+ * blackwell_gemm_ws.py:24-341).  Fields the caller set to non-zero are kept. */
+B2X_API b2x_status b2x_gemm_default_config(const b2x_gemm_args* args, b2x_gemm_config* out);
+B2X_API size_t b2x_gemm_workspace_size(const b2x_gemm_args* args);
+B2X_API b2x_status b2x_fp8_gemm(const b2x_gemm_args* args, void* stream);
+
+/*
+ * Reference-compatible split-K reduce: c[m,n] = cast(sum_s ws[s*M + m, n]),
+ * summed in fp32.  ws is [split_k*M, N] of ws_type (row stride N), c is
+ * [M,N] of c_type (row stride ldc).
+ * Replaces: _reduce_k_kernel, blackwell_gemm_ws.py:1033-1056.
+ */
+B2X_API b2x_status b2x_splitk_reduce(const void* ws, b2x_dtype ws_type, void* c, b2x_dtype c_type, int64_t M, int64_t N,
+                             int64_t ldc, int split_k, void* stream);
+
+/* ------------------------------------------------------------------ misc */
+
+/* Message for the calling thread's last failed call ("" if none). */
+B2X_API const char* b2x_last_error(void);
+/* Reads and clears the device status word of the current device (blocking). */
+B2X_API b2x_status b2x_read_device_status(int* status_out);
+/* ABI version of the loaded library (B2X_ABI_VERSION). */
+B2X_API int b2x_abi_version(void);
+/* Number of kernels this library launched since load (all devices). */
+B2X_API uint64_t b2x_launch_count(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* B2X_H_ */

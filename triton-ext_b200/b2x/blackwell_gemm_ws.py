@@ -1,0 +1,384 @@
+"""Drop-in counterpart of the reference's Blackwell warp-specialized GEMM module
+(extensions/utlx/tlx/tutorials/blackwell_gemm_ws.py), for fp8 operands.
+
+Same public names and argument order:
+    matmul(a, b, config=None, use_heuristic=False)          (:1352)
+    get_heuristic_config(M, N, K, num_sms=148)               (:24)
+    _select_group_size_m(M, N, block_m)                      (:344)
+    get_cuda_autotune_config()                               (:371)
+    matmul_tma_set_block_size_hook(nargs)                    (:401)
+    preprocess_configs(configs, named_args, **kwargs)        (:442)
+    reduce_k(workspace, c, M, N, SPLIT_K)  ~ _reduce_k_kernel (:1033)
+The work runs in libb2x's sm_100a kernels: a persistent warp-specialized
+tcgen05 GEMM with TMEM accumulators (producer warp, MMA warp, two ping-ponged
+epilogue warpgroups), split-K reduced in fp32 with red.global.add.
+
+Differences a caller can see:
+* a and b are float8 (e4m3fn / e5m2).  The reference returns C in a.dtype;
+  for fp8 inputs b2x returns bfloat16 (or `out_dtype`), because an fp8
+  output of an fp8 GEMM is not what fp8 inference wants.  fp16/bf16 inputs
+  raise NotImplementedError: that GEMM is outside this library's path.
+* Optional keyword-only scale_a / scale_b: scalars (per-tensor, C = sA*sB*A.B)
+  or 2-D block scales (A: [M, ceil(K/128)], B: [ceil(K/128), ceil(N/128)]).
+* The CTA tile is 128 x BLOCK_SIZE_N x 128; config keys BLOCK_SIZE_M (128 or
+  256), NUM_MMA_GROUPS, NUM_CTAS, NUM_SMEM_BUFFERS, NUM_TMEM_BUFFERS,
+  EPILOGUE_SUBTILE, INTERLEAVE_EPILOGUE and USE_WARP_BARRIER are accepted and
+  mapped (BLOCK_SIZE_M=256 doubles GROUP_SIZE_M so the tile order covers the
+  same rows); the ring depth is always the deepest that fits in 227 KB.
+"""
+from __future__ import annotations
+
+import functools
+import math
+import os
+import warnings
+from typing import Optional
+
+import torch
+
+from . import ops
+
+_printed_heuristic_configs = set()
+_autotune_cache: dict = {}
+
+
+@functools.lru_cache(maxsize=None)
+def _get_num_sms(device_index: int = 0) -> int:
+    return torch.cuda.get_device_properties(device_index).multi_processor_count
+
+
+# ----------------------------------------------------------------------------
+# Heuristics (restated from the reference; same rules, same returned keys).
+
+
+def _select_group_size_m(M, N, block_m):
+    """Tile-order group size: sweep M when M >> N, sweep N when N >> M (:344-368)."""
+    num_m_tiles = (M + block_m - 1) // block_m
+    ratio = M / max(N, 1)
+    if ratio > 10:
+        return 1
+    if ratio < 0.1:
+        return min(64, num_m_tiles)
+    return min(8, num_m_tiles)
+
+
+def _cfg(bm, bn, bk, g, s, t, m, sub, ctas, sk, inter):
+    return {
+        "BLOCK_SIZE_M": bm, "BLOCK_SIZE_N": bn, "BLOCK_SIZE_K": bk, "GROUP_SIZE_M": g,
+        "NUM_SMEM_BUFFERS": s, "NUM_TMEM_BUFFERS": t, "NUM_MMA_GROUPS": m, "EPILOGUE_SUBTILE": sub,
+        "NUM_CTAS": ctas, "SPLIT_K": sk, "INTERLEAVE_EPILOGUE": inter,
+        "ctas_per_cga": (ctas, 1, 1) if ctas > 1 else None,
+        "pre_hook": matmul_tma_set_block_size_hook,
+    }
+
+
+# (BLOCK_M, BLOCK_N, BLOCK_K, NUM_CTAS, SMEM_BUFS, TMEM_BUFS, MMA_GROUPS, SUBTILE) candidates of the
+# wave-efficiency fallback (:197-222).
+_FALLBACK_CANDIDATES = (
+    (256, 128, 128, 2, 2, 2, 2, 1), (256, 256, 64, 1, 3, 1, 2, 4), (128, 64, 128, 1, 4, 3, 2, 1),
+    (256, 128, 64, 2, 5, 2, 2, 4), (128, 256, 64, 2, 4, 2, 1, 2), (256, 64, 128, 2, 5, 2, 2, 4),
+    (128, 64, 128, 2, 5, 2, 2, 1), (256, 64, 128, 1, 5, 2, 2, 8), (128, 256, 64, 1, 3, 2, 1, 2),
+    (128, 128, 64, 1, 4, 2, 1, 2), (256, 128, 64, 1, 3, 1, 2, 2), (128, 64, 64, 1, 5, 2, 1, 1),
+    (64, 128, 64, 1, 5, 2, 1, 1), (64, 64, 64, 1, 6, 2, 1, 1),
+)
+
+
+def get_heuristic_config(M, N, K, num_sms=148):
+    """Shape-rule config selection (the rules of blackwell_gemm_ws.py:24-341).
+
+    1. Tall-M (M/N > 4) shapes that fill the GPU: 256-row tiles in CTA pairs.
+    2. Shapes whose tiles cannot fill the GPU: split-K (first of 4, 2, 8 that
+       leaves >= 4 K tiles per split).
+    3. Other shapes that fill the GPU: 256 x 256 x 64.
+    4. Otherwise the candidate with the best last-wave occupancy.
+    """
+    max_smem, max_tmem = 232 * 1024, 256 * 1024
+    ratio = M / max(N, 1)
+    tall_m, tall_n = ratio > 4, ratio < 0.25
+    rbm, rbn = (256, 128) if tall_m else ((128, 256) if tall_n else (256, 256))
+    mn_tiles = math.ceil(M / rbm) * math.ceil(N / rbn)
+    saturated = mn_tiles >= num_sms
+
+    if tall_m and saturated:
+        if K / max(min(M, N), 1) <= 1.5:
+            return _cfg(256, 128, 128, _select_group_size_m(M, N, 256), 2, 2, 2, 1, 2, 1, 1)
+        if K > N * 2:
+            return _cfg(256, 256, 128, _select_group_size_m(M, N, 256), 2, 1, 2, 4, 2, 1, 0)
+        return _cfg(256, 256, 64, _select_group_size_m(M, N, 256), 4, 1, 2, 4, 2, 1, 1)
+
+    if not saturated:
+        large_out = M * N >= 1_000_000
+        bm, bn, bk = (256, 128, 64) if large_out else (128, 64, 128)
+        k_tiles = math.ceil(K / bk)
+        split_k = next((sk for sk in (4, 2, 8) if k_tiles >= sk and k_tiles // sk >= 4), 1)
+        if split_k > 1:
+            if large_out:
+                return _cfg(bm, bn, bk, _select_group_size_m(M, N, bm), 4, 2, 2, 8, 1, split_k, 1)
+            return _cfg(bm, bn, bk, _select_group_size_m(M, N, bm), 4, 3, 2, 1, 1, split_k, 1)
+
+    if saturated:
+        return _cfg(256, 256, 64, _select_group_size_m(M, N, 256), 3, 1, 2, 4, 1, 1, 1)
+
+    def smem_bytes(bm, bn, bk, ctas, s, g, sub):
+        return bm * bk * 2 * s + bk * (bn // ctas) * 2 * s + bm * (bn // sub) * 2 + s * g * 8 * (2 if ctas == 2 else 1)
+
+    def wave(bm, bn, ctas, sk=1):
+        cm = (M + bm - 1) // bm
+        cm = (cm + ctas - 1) // ctas * ctas
+        total = cm * ((N + bn - 1) // bn) * sk
+        if total == 0:
+            return float("inf"), 0, 0
+        waves = (total + num_sms - 1) // num_sms
+        return waves - total / num_sms, total, waves
+
+    best, best_score, best_waves = None, float("inf"), float("inf")
+    for bm, bn, bk, ctas, s, t, g, sub in _FALLBACK_CANDIDATES:
+        if smem_bytes(bm, bn, bk, ctas, s, g, sub) > max_smem or bm * bn * 4 * t > max_tmem:
+            continue
+        if bm // g > 128 or bm > M * 2 or bn > N * 2:
+            continue
+        score, total, waves = wave(bm, bn, ctas)
+        split_k = 1
+        if math.ceil(M / bm) * math.ceil(N / bn) < num_sms:
+            k_tiles = math.ceil(K / bk)
+            for sk in (8, 4, 2):
+                if k_tiles >= sk and k_tiles // sk >= 4:
+                    s2, t2, w2 = wave(bm, bn, ctas, sk)
+                    if s2 < score or (s2 == score and t2 > total):
+                        score, total, waves, split_k = s2, t2, w2, sk
+                    break
+        slack = 0.1
+        if (score < best_score - slack or (score < best_score + slack and waves < best_waves)
+                or (score < best_score + slack and waves == best_waves and ctas > 1)):
+            best_score, best_waves = score, waves
+            best = _cfg(bm, bn, bk, _select_group_size_m(M, N, bm), s, t, g, sub, ctas, split_k, 0)
+    return best
+
+
+def get_cuda_autotune_config():
+    """The reference's config space (:371-398), as plain dicts."""
+    out = []
+    for BM in (128, 256):
+        for BN in (64, 128, 256):
+            for BK in (64, 128):
+                for s in (2, 3, 4, 5, 6, 7):
+                    for t in (1, 2, 3):
+                        for m in (1, 2):
+                            for sub in (1, 2, 4, 8):
+                                for ctas in (1, 2):
+                                    for sk in (1, 2, 3, 4, 5, 6, 8, 10, 12, 16, 19, 24):
+                                        for inter in (0, 1):
+                                            for g in (1, 8, 64):
+                                                for uwb in (False, True):
+                                                    d = _cfg(BM, BN, BK, g, s, t, m, sub, ctas, sk, inter)
+                                                    d["USE_WARP_BARRIER"] = uwb
+                                                    out.append(d)
+    return out
+
+
+def matmul_tma_set_block_size_hook(nargs):
+    """Descriptor block shapes (:401-429).  b2x builds its TMA descriptors in
+    C++ from the config; this records the shapes the reference would use."""
+    bm, bn, bk = nargs["BLOCK_SIZE_M"], nargs["BLOCK_SIZE_N"], nargs["BLOCK_SIZE_K"]
+    g, ctas, sub = nargs.get("NUM_MMA_GROUPS", 1), nargs.get("NUM_CTAS", 1), nargs.get("EPILOGUE_SUBTILE", 1)
+    nargs["a_block_shape"] = [bm // g, bk]
+    nargs["b_block_shape"] = [bk, bn // ctas]
+    nargs["c_block_shape"] = [bm // g, bn // sub]
+    return nargs
+
+
+def preprocess_configs(configs, named_args, **kwargs):
+    """Autotune pruning (:442-637): hardware budgets, split-K gating, wave
+    count, GROUP_SIZE_M rule and the Pareto filter on buffer counts.
+    Accepts dicts or objects with a `.kwargs` dict; returns the survivors."""
+    num_sms = kwargs.get("num_sms") or (_get_num_sms() if torch.cuda.is_available() else 148)
+    M, N, K = named_args["M"], named_args["N"], named_args["K"]
+
+    def kw(c):
+        return c.kwargs if hasattr(c, "kwargs") else c
+
+    kept = []
+    for c in configs:
+        k = kw(c)
+        bm, bn, bk = k["BLOCK_SIZE_M"], k["BLOCK_SIZE_N"], k["BLOCK_SIZE_K"]
+        s, t, ctas, g = k["NUM_SMEM_BUFFERS"], k["NUM_TMEM_BUFFERS"], k["NUM_CTAS"], k["NUM_MMA_GROUPS"]
+        sk, sub, inter, gsm = k.get("SPLIT_K", 1), k["EPILOGUE_SUBTILE"], k.get("INTERLEAVE_EPILOGUE", 0), k["GROUP_SIZE_M"]
+        if bm // g > 128 or (ctas == 2 and bm // g == 64) or gsm % ctas or bn % sub or (inter and g != 2):
+            continue
+        mn_tiles = math.ceil(M / bm) * math.ceil(N / bn)
+        if sk > 1:
+            k_tiles = math.ceil(K / bk)
+            if mn_tiles >= num_sms or k_tiles < sk or k_tiles // sk < 4:
+                continue
+        smem = bm * bk * 2 * s + bk * (bn // ctas) * 2 * s + bm * (bn // sub) * 2
+        smem += s * g * 8 * (2 if ctas == 2 else 1) + t
+        if smem > 232 * 1024 or bm * bn * 4 * t > 256 * 1024:
+            continue
+        kept.append(c)
+
+    def tiles(c):
+        k = kw(c)
+        return math.ceil(M / k["BLOCK_SIZE_M"]) * math.ceil(N / k["BLOCK_SIZE_N"]) * k.get("SPLIT_K", 1)
+
+    groups = {}
+    for c in kept:
+        k = kw(c)
+        groups.setdefault((k["BLOCK_SIZE_M"], k["BLOCK_SIZE_N"], k["BLOCK_SIZE_K"]), []).append(c)
+    kept = []
+    for members in groups.values():
+        waves = {id(c): math.ceil(tiles(c) / num_sms) for c in members}
+        lo = min(waves.values())
+        best = [c for c in members if waves[id(c)] == lo]
+        top = max(kw(c).get("SPLIT_K", 1) for c in best)
+        kept.extend(c for c in best if kw(c).get("SPLIT_K", 1) == top)
+
+    if kept:
+        if M > N * 10:
+            kept = [c for c in kept if kw(c)["GROUP_SIZE_M"] == 1]
+        elif N > M * 10:
+            kept = [c for c in kept if kw(c)["GROUP_SIZE_M"] >= 32]
+        else:
+            kept = [c for c in kept if kw(c)["GROUP_SIZE_M"] == 8]
+
+    def gkey(c):
+        k = kw(c)
+        return (k["BLOCK_SIZE_M"], k["BLOCK_SIZE_N"], k["BLOCK_SIZE_K"], k["EPILOGUE_SUBTILE"], k["NUM_CTAS"],
+                k.get("SPLIT_K", 1), k.get("INTERLEAVE_EPILOGUE", 0))
+
+    def val(c):
+        k = kw(c)
+        return (k["NUM_SMEM_BUFFERS"], k["NUM_TMEM_BUFFERS"], k["NUM_MMA_GROUPS"])
+
+    def dominates(x, y):
+        vx, vy = val(x), val(y)
+        return all(p >= q for p, q in zip(vx, vy)) and any(p > q for p, q in zip(vx, vy))
+
+    pg = {}
+    for c in kept:
+        pg.setdefault(gkey(c), []).append(c)
+    return [c for ms in pg.values() for c in ms if not any(dominates(o, c) for o in ms if o is not c)]
+
+
+# ----------------------------------------------------------------------------
+# matmul
+
+
+def _to_b2x_config(cfg: dict, K: int) -> list:
+    """Reference config dict -> b2x_gemm_config fields (see module docstring)."""
+    bm = int(cfg.get("BLOCK_SIZE_M", 128))
+    bn = int(cfg.get("BLOCK_SIZE_N", 0))
+    if bn and bn not in (64, 128, 256):
+        bn = min((64, 128, 256), key=lambda v: abs(v - bn))
+    group = int(cfg.get("GROUP_SIZE_M", 0)) * max(1, bm // 128)
+    sk = max(1, int(cfg.get("SPLIT_K", 1)))
+    k_tiles = -(-K // 128)
+    while sk > 1 and (k_tiles < sk or (sk - 1) * -(-k_tiles // sk) >= k_tiles):
+        sk -= 1
+    if sk != int(cfg.get("SPLIT_K", 1)):
+        warnings.warn(f"SPLIT_K={cfg.get('SPLIT_K')} leaves empty splits over {k_tiles} K blocks of 128; "
+                      f"using SPLIT_K={sk}", stacklevel=3)
+    return [128, bn, 128, group, 0, int(cfg.get("NUM_TMEM_BUFFERS", 2)), int(cfg.get("NUM_MMA_GROUPS", 1)),
+            int(cfg.get("EPILOGUE_SUBTILE", 1)), int(cfg.get("NUM_CTAS", 1)), sk,
+            int(cfg.get("INTERLEAVE_EPILOGUE", 0))]
+
+
+def _scale_mode(scale_a, scale_b) -> str:
+    if scale_a is None and scale_b is None:
+        return "none"
+    if scale_a is None or scale_b is None:
+        raise ValueError("pass both scale_a and scale_b, or neither")
+    if scale_a.numel() == 1 and scale_b.numel() == 1:
+        return "tensor"
+    if scale_a.dim() == 2 and scale_b.dim() == 2:
+        return "block"
+    raise ValueError("scales must both be one-element tensors or both 2-D block-scale tensors")
+
+
+def _autotune(a, b, scale_a, scale_b, mode, out_dtype):
+    """First call per problem: time the default choice against its neighbours
+    and keep the fastest (the role of @triton.autotune, :1459-1464)."""
+    M, K = a.shape
+    N = b.shape[1]
+    key = (M, N, K, a.dtype, b.dtype, b.stride(), mode, out_dtype, a.device.index)
+    if key in _autotune_cache:
+        return _autotune_cache[key]
+    base = ops.gemm_config(a, b, mode)
+    cands = [[0] * 11]
+    if mode != "block":
+        row_major_b = b.stride(1) == 1 and b.stride(0) != 1
+        for bn in (256, 128, 64):
+            if row_major_b and bn < 128:
+                continue
+            for sk in sorted({1, base["split_k"]}):
+                c = [0] * 11
+                c[1], c[9] = bn, sk
+                if c not in cands:
+                    cands.append(c)
+    if len(cands) == 1 or os.environ.get("B2X_AUTOTUNE", "1") == "0":
+        _autotune_cache[key] = cands[0]
+        return cands[0]
+    best, best_t = cands[0], float("inf")
+    for c in cands:
+        try:
+            ops.fp8_gemm_op(a, b, scale_a, scale_b, mode, out_dtype, c)
+        except Exception:
+            continue
+        st, en = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        st.record()
+        for _ in range(3):
+            ops.fp8_gemm_op(a, b, scale_a, scale_b, mode, out_dtype, c)
+        en.record()
+        en.synchronize()
+        t = st.elapsed_time(en)
+        if t < best_t:
+            best, best_t = c, t
+    _autotune_cache[key] = best
+    return best
+
+
+def matmul(a, b, config=None, use_heuristic=False, *, scale_a: Optional[torch.Tensor] = None,
+           scale_b: Optional[torch.Tensor] = None, out_dtype: Optional[torch.dtype] = None):
+    """C = A @ B for float8 A (M, K) and B (K, N); see the module docstring.
+
+    config: a reference-style config dict (keys BLOCK_SIZE_N, GROUP_SIZE_M,
+    SPLIT_K, ... ; `ctas_per_cga` and `pre_hook` are ignored).  None with
+    use_heuristic=True takes get_heuristic_config(); None otherwise autotunes
+    once per shape.
+    """
+    assert a.shape[1] == b.shape[0], "Incompatible dimensions"
+    assert a.is_contiguous(), "Matrix A must be contiguous"
+    if a.dtype not in ops.FP8_DTYPES or b.dtype not in ops.FP8_DTYPES:
+        raise NotImplementedError(
+            f"b2x implements the fp8 GEMM path (float8_e4m3fn / float8_e5m2); got {a.dtype} x {b.dtype}")
+    M, K = a.shape
+    N = b.shape[1]
+    out_dtype = out_dtype or torch.bfloat16
+    mode = _scale_mode(scale_a, scale_b)
+    if scale_a is not None and mode == "tensor":
+        scale_a = scale_a.reshape(1).to(torch.float32)
+        scale_b = scale_b.reshape(1).to(torch.float32)
+    if config is None and use_heuristic:
+        config = get_heuristic_config(M, N, K, _get_num_sms(a.device.index or 0))
+        if config is not None and os.environ.get("TRITON_PRINT_AUTOTUNING") == "1" and (M, N, K) not in _printed_heuristic_configs:
+            _printed_heuristic_configs.add((M, N, K))
+            s = ", ".join(f"{k}: {v}" for k, v in config.items() if k not in ("pre_hook", "ctas_per_cga"))
+            print(f"heuristic config selected: {s};")
+    if config is not None:
+        cfg = dict(config)
+        cfg.pop("ctas_per_cga", None)
+        cfg.pop("pre_hook", None)
+        if mode == "block":
+            cfg["BLOCK_SIZE_N"], cfg["SPLIT_K"] = 128, 1
+        fields = _to_b2x_config(cfg, K)
+    else:
+        fields = _autotune(a, b, scale_a, scale_b, mode, out_dtype)
+    return ops.fp8_gemm_op(a, b, scale_a, scale_b, mode, out_dtype, fields)
+
+
+def reduce_k(workspace, c, M, N, SPLIT_K):
+    """c[m, n] = sum_s workspace[s*M + m, n] in fp32, stored in c.dtype (:1033-1056)."""
+    ops.reduce_k_op(workspace, c, M, N, SPLIT_K)
+    return c
+
+
+_reduce_k_kernel = reduce_k

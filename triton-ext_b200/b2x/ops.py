@@ -1,0 +1,277 @@
+"""Torch-facing ops over the libb2x C ABI, registered as torch custom ops
+(`torch.ops.b2x.quantize`, `torch.ops.b2x.fp8_gemm`, `torch.ops.b2x.reduce_k`).
+
+Torch is used here only for device memory, the current stream and the op
+registry.  All arithmetic happens in the sm_100a kernels of libb2x.so.
+"""
+from __future__ import annotations
+
+import ctypes
+import threading
+from typing import Optional, Sequence
+
+import torch
+
+from . import _lib as L
+
+FP8_DTYPES = {torch.float8_e4m3fn: L.E4M3, torch.float8_e5m2: L.E5M2}
+IN_DTYPES = {torch.float32: L.F32, torch.bfloat16: L.BF16}
+OUT_DTYPES = {torch.bfloat16: L.BF16, torch.float16: L.F16}
+CAST_MODES = {
+    "none": L.SCALE_NONE,
+    "tensor": L.SCALE_TENSOR,
+    "given": L.SCALE_TENSOR_GIVEN,
+    "block1x128": L.SCALE_BLOCK_1x128,
+    "block128x128": L.SCALE_BLOCK_128x128,
+    "mx1x32": L.SCALE_MX_1x32,
+}
+GEMM_SCALE_MODES = {"none": L.SCALE_NONE, "tensor": L.SCALE_TENSOR, "block": L.SCALE_BLOCK_1x128}
+CONFIG_FIELDS = ("block_m", "block_n", "block_k", "group_size_m", "num_smem_buffers", "num_tmem_buffers",
+                 "num_mma_groups", "epilogue_subtile", "num_ctas", "split_k", "interleave_epilogue")
+
+
+def _ptr(t: Optional[torch.Tensor]) -> Optional[int]:
+    return None if t is None else t.data_ptr()
+
+
+def _stream(dev: torch.device) -> int:
+    return torch.cuda.current_stream(dev).cuda_stream
+
+
+def _require_cuda(*ts: torch.Tensor) -> None:
+    for t in ts:
+        if t is not None and not t.is_cuda:
+            raise ValueError("b2x ops take CUDA tensors only (there is no CPU path)")
+
+
+# ----------------------------------------------------------------------------
+# Workspaces.  Split-K workspaces must be all-zero before a call and are
+# returned all-zero by every successful call, so one zeroed buffer per
+# (device, stream) is reused; it is dropped after any failed call.
+
+_ws_lock = threading.Lock()
+_ws_cache: dict = {}
+
+
+def _workspace(dev: torch.device, nbytes: int, zeroed: bool) -> torch.Tensor:
+    key = (dev.index, _stream(dev), zeroed)
+    with _ws_lock:
+        buf = _ws_cache.get(key)
+        if buf is None or buf.numel() < nbytes:
+            buf = torch.zeros(max(nbytes, 256), dtype=torch.uint8, device=dev)
+            _ws_cache[key] = buf
+        return buf
+
+
+def _drop_workspaces() -> None:
+    with _ws_lock:
+        _ws_cache.clear()
+
+
+# ----------------------------------------------------------------------------
+# quantize
+
+
+def _scale_shape(mode: str, R: int, C: int):
+    if mode in ("tensor", "given"):
+        return (1,), torch.float32
+    if mode == "block1x128":
+        return (R, -(-C // 128)), torch.float32
+    if mode == "block128x128":
+        return (-(-R // 128), -(-C // 128)), torch.float32
+    if mode == "mx1x32":
+        return (R, -(-C // 32)), torch.uint8
+    return (0,), torch.float32
+
+
+@torch.library.custom_op("b2x::quantize", mutates_args=())
+def quantize_op(x: torch.Tensor, mode: str, fp8_dtype: torch.dtype,
+                scale: Optional[torch.Tensor] = None) -> tuple[torch.Tensor, torch.Tensor]:
+    """fp32/bf16 [R, C] -> (fp8 [R, C], scales); see include/b2x.h b2x_fp8_cast."""
+    _require_cuda(x, scale)
+    if mode not in CAST_MODES:
+        raise ValueError(f"unknown quantize mode {mode!r}; expected one of {sorted(CAST_MODES)}")
+    if x.dtype not in IN_DTYPES:
+        raise TypeError(f"quantize input must be float32 or bfloat16, got {x.dtype}")
+    if fp8_dtype not in FP8_DTYPES:
+        raise TypeError(f"quantize output must be float8_e4m3fn or float8_e5m2, got {fp8_dtype}")
+    x2 = x.reshape(1, -1) if x.dim() == 1 else x
+    if x2.dim() != 2:
+        x2 = x2.reshape(-1, x2.shape[-1])
+    if x2.stride(-1) != 1:
+        x2 = x2.contiguous()
+    R, C = x2.shape
+    q = torch.empty((R, C), dtype=fp8_dtype, device=x.device)
+    sshape, sdt = _scale_shape(mode, R, C)
+    if mode == "given":
+        if scale is None:
+            raise ValueError("mode 'given' needs a scale tensor")
+        sc = scale.to(torch.float32).reshape(1).contiguous()
+    else:
+        sc = torch.empty(sshape, dtype=sdt, device=x.device)
+    a = L.CastArgs()
+    a.x, a.x_type, a.rows, a.cols, a.ld_x = x2.data_ptr(), IN_DTYPES[x.dtype], R, C, x2.stride(0)
+    a.q, a.q_type, a.ld_q = q.data_ptr(), FP8_DTYPES[fp8_dtype], C
+    a.scale = sc.data_ptr() if sc.numel() else None
+    a.mode = CAST_MODES[mode]
+    a.ld_scale = sc.shape[1] if sc.dim() == 2 else 1
+    lib = L.lib()
+    nws = lib.b2x_cast_workspace_size(ctypes.byref(a))
+    if nws:
+        ws = _workspace(x.device, nws, zeroed=False)
+        a.workspace, a.workspace_bytes = ws.data_ptr(), ws.numel()
+    with torch.cuda.device(x.device):
+        L.check(lib.b2x_fp8_cast(ctypes.byref(a), ctypes.c_void_p(_stream(x.device))))
+    return q.reshape(x.shape), sc
+
+
+@quantize_op.register_fake
+def _(x, mode, fp8_dtype, scale=None):
+    x2 = x.reshape(-1, x.shape[-1]) if x.dim() != 1 else x.reshape(1, -1)
+    sshape, sdt = _scale_shape(mode, x2.shape[0], x2.shape[1])
+    return torch.empty_like(x, dtype=fp8_dtype), x.new_empty(sshape, dtype=sdt)
+
+
+def amax(x: torch.Tensor) -> torch.Tensor:
+    """NaN-ignoring max |x| on the GPU (one fp32 element)."""
+    _require_cuda(x)
+    x2 = x.reshape(1, -1) if x.dim() == 1 else x.reshape(-1, x.shape[-1])
+    if x2.stride(-1) != 1:
+        x2 = x2.contiguous()
+    out = torch.empty(1, dtype=torch.float32, device=x.device)
+    a = L.CastArgs()
+    a.rows, a.cols, a.ld_x, a.ld_q, a.mode = x2.shape[0], x2.shape[1], x2.stride(0), x2.stride(0), L.SCALE_TENSOR
+    lib = L.lib()
+    ws = _workspace(x.device, lib.b2x_cast_workspace_size(ctypes.byref(a)), zeroed=False)
+    with torch.cuda.device(x.device):
+        L.check(lib.b2x_amax(x2.data_ptr(), IN_DTYPES[x.dtype], x2.shape[0], x2.shape[1], x2.stride(0),
+                             out.data_ptr(), ws.data_ptr(), ws.numel(), ctypes.c_void_p(_stream(x.device))))
+    return out
+
+
+# ----------------------------------------------------------------------------
+# GEMM
+
+
+def _gemm_args(a, b, c, scale_mode, scale_a, scale_b, config: Sequence[int]) -> L.GemmArgs:
+    M, K = a.shape
+    K2, N = b.shape
+    g = L.GemmArgs()
+    g.a, g.b, g.c = a.data_ptr(), b.data_ptr(), c.data_ptr()
+    g.M, g.N, g.K = M, N, K
+    g.lda = a.stride(0)
+    sk, sn = b.stride()
+    if sk == 1 and (sn != 1 or N == 1):
+        g.ldb_k, g.ldb_n = 1, (sn if N > 1 else max(K, 16))
+    else:
+        g.ldb_k, g.ldb_n = (sk if K > 1 else max(N, 16)), sn
+    g.ldc = c.stride(0)
+    g.a_type, g.b_type, g.c_type = FP8_DTYPES[a.dtype], FP8_DTYPES[b.dtype], OUT_DTYPES[c.dtype]
+    g.scale_mode = GEMM_SCALE_MODES[scale_mode]
+    if scale_a is not None:
+        g.scale_a = scale_a.data_ptr()
+        if scale_a.dim() == 2:
+            g.sa_stride_m, g.sa_stride_k = scale_a.stride()
+    if scale_b is not None:
+        g.scale_b = scale_b.data_ptr()
+        if scale_b.dim() == 2:
+            g.sb_stride_k, g.sb_stride_n = scale_b.stride()
+    for name, v in zip(CONFIG_FIELDS, config):
+        setattr(g.config, name, int(v))
+    return g
+
+
+def _tma_friendly(a: torch.Tensor, b: torch.Tensor):
+    """TMA descriptors need 16-byte aligned bases and row pitches.  Operands
+    that miss this (K or N not a multiple of 16, odd views) are copied once
+    into zero-padded buffers; the padding adds zero products only."""
+    M, K = a.shape
+    N = b.shape[1]
+    k16 = -(-K // 16) * 16
+    a_ok = a.stride(1) == 1 and a.stride(0) % 16 == 0 and a.data_ptr() % 16 == 0 and K % 16 == 0
+    if not a_ok:
+        ap = torch.zeros((M, k16), dtype=a.dtype, device=a.device)
+        ap[:, :K] = a
+        a = ap
+    sk, sn = b.stride()
+    kmajor = sk == 1 and (sn != 1 or N == 1)
+    if kmajor:
+        b_ok = sn % 16 == 0 and b.data_ptr() % 16 == 0 and K % 16 == 0
+    else:
+        b_ok = sn == 1 and sk % 16 == 0 and b.data_ptr() % 16 == 0 and K % 16 == 0
+    if not b_ok:
+        # store as an [N, K16] K-major weight (the layout the kernel streams best)
+        bp = torch.zeros((N, k16), dtype=b.dtype, device=b.device)
+        bp[:, :K] = b.t()
+        b = bp.t()
+    return a, b
+
+
+@torch.library.custom_op("b2x::fp8_gemm", mutates_args=())
+def fp8_gemm_op(a: torch.Tensor, b: torch.Tensor, scale_a: Optional[torch.Tensor], scale_b: Optional[torch.Tensor],
+                scale_mode: str, out_dtype: torch.dtype, config: list[int]) -> torch.Tensor:
+    """C[M,N] = scaled fp8 A[M,K] @ B[K,N]; see include/b2x.h b2x_fp8_gemm."""
+    _require_cuda(a, b, scale_a, scale_b)
+    if a.dtype not in FP8_DTYPES or b.dtype not in FP8_DTYPES:
+        raise TypeError(f"fp8_gemm takes float8 A and B, got {a.dtype} and {b.dtype}")
+    if out_dtype not in OUT_DTYPES:
+        raise TypeError(f"fp8_gemm output must be bfloat16 or float16, got {out_dtype}")
+    M, K = a.shape
+    N = b.shape[1]
+    if M == 0 or N == 0:
+        return torch.empty((M, N), dtype=out_dtype, device=a.device)
+    a, b = _tma_friendly(a, b)
+    # TMA needs 16-byte row pitches: give C a padded pitch when N % 8 != 0.
+    n8 = -(-N // 8) * 8
+    c = torch.empty((M, n8), dtype=out_dtype, device=a.device)[:, :N]
+    g = _gemm_args(a, b, c, scale_mode, scale_a, scale_b, config)
+    lib = L.lib()
+    with torch.cuda.device(a.device):
+        nws = lib.b2x_gemm_workspace_size(ctypes.byref(g))
+        if nws:
+            ws = _workspace(a.device, nws, zeroed=True)
+            g.workspace, g.workspace_bytes = ws.data_ptr(), ws.numel()
+        st = lib.b2x_fp8_gemm(ctypes.byref(g), ctypes.c_void_p(_stream(a.device)))
+        if st != L.OK:
+            _drop_workspaces()
+        L.check(st)
+    return c
+
+
+@fp8_gemm_op.register_fake
+def _(a, b, scale_a, scale_b, scale_mode, out_dtype, config):
+    return a.new_empty((a.shape[0], b.shape[1]), dtype=out_dtype)
+
+
+def gemm_config(a: torch.Tensor, b: torch.Tensor, scale_mode: str = "tensor",
+                config: Sequence[int] = ()) -> dict:
+    """The configuration libb2x picks for this problem (all fields filled)."""
+    c = torch.empty((1, 1), dtype=torch.bfloat16, device=a.device)
+    g = _gemm_args(a, b, c, scale_mode, None, None, tuple(config) + (0,) * (len(CONFIG_FIELDS) - len(config)))
+    g.M, g.N = a.shape[0], b.shape[1]
+    out = L.GemmConfig()
+    L.check(L.lib().b2x_gemm_default_config(ctypes.byref(g), ctypes.byref(out)))
+    return {n: getattr(out, n) for n in CONFIG_FIELDS}
+
+
+@torch.library.custom_op("b2x::reduce_k", mutates_args=("c",))
+def reduce_k_op(workspace: torch.Tensor, c: torch.Tensor, M: int, N: int, SPLIT_K: int) -> None:
+    """c = cast(sum over SPLIT_K planes of workspace[(SPLIT_K*M), N]) (fp32 sum)."""
+    _require_cuda(workspace, c)
+    dt = {torch.float32: L.F32, torch.bfloat16: L.BF16, torch.float16: L.F16}
+    if workspace.dtype not in dt or c.dtype not in dt:
+        raise TypeError("reduce_k supports float32 / bfloat16 / float16")
+    if workspace.numel() < SPLIT_K * M * N or not workspace.is_contiguous():
+        raise ValueError("workspace must be a contiguous (SPLIT_K*M, N) tensor")
+    if c.stride(-1) != 1:
+        raise ValueError("c must have unit column stride")
+    with torch.cuda.device(c.device):
+        L.check(L.lib().b2x_splitk_reduce(workspace.data_ptr(), dt[workspace.dtype], c.data_ptr(), dt[c.dtype],
+                                          M, N, c.stride(0), SPLIT_K, ctypes.c_void_p(_stream(c.device))))
+
+
+def quantize(x: torch.Tensor, mode: str = "tensor", dtype: torch.dtype = torch.float8_e4m3fn,
+             scale: Optional[torch.Tensor] = None):
+    """Quantize fp32/bf16 to fp8. Returns (q, scale) -- scale is None for mode 'none'."""
+    q, sc = torch.ops.b2x.quantize(x, mode, dtype, scale)
+    return q, (None if mode == "none" else sc)

@@ -1,0 +1,440 @@
+// C ABI of libb2x: argument validation, configuration, TMA descriptors and
+// kernel launch.  No exception crosses this boundary; every entry point
+// returns a b2x_status and records a message for b2x_last_error().
+//
+// Counterpart of the host side of matmul() (extensions/utlx/tlx/tutorials/
+// blackwell_gemm_ws.py:1352-1483): the shape asserts (:1368-1369), the
+// descriptor set-up (:1377-1379, matmul_tma_set_block_size_hook :401-429), the
+// persistent grid min(NUM_SMS, tiles) (:1430) and the split-K gating of
+// preprocess_configs (:487-497).
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <cudaTypedefs.h>
+#include <atomic>
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+#include <unordered_map>
+#include <utility>
+#include "b2x_internal.h"
+#include "b2x_ptx.cuh"
+
+namespace b2x {
+
+static thread_local char t_err[512] = {0};
+static std::atomic<uint64_t> g_launches{0};
+
+void note_launch(int n) { g_launches.fetch_add((uint64_t)n, std::memory_order_relaxed); }
+
+static b2x_status fail(b2x_status s, const char* fmt, ...) {
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(t_err, sizeof(t_err), fmt, ap);
+  va_end(ap);
+  return s;
+}
+
+static b2x_status cuda_fail(cudaError_t e, const char* what) {
+  return fail(B2X_ERR_CUDA, "%s: %s (%s)", what, cudaGetErrorName(e), cudaGetErrorString(e));
+}
+
+static std::mutex g_mu;
+static std::unordered_map<int, int> g_num_sms;
+static std::unordered_map<uint64_t, int> g_smem_attr;  // key: (device << 48) ^ func
+
+static int device_num_sms(int dev) {
+  std::lock_guard<std::mutex> lk(g_mu);
+  auto it = g_num_sms.find(dev);
+  if (it != g_num_sms.end()) return it->second;
+  int n = 148;
+  cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+  g_num_sms[dev] = n;
+  return n;
+}
+
+cudaError_t ensure_smem_attr(const void* func, int bytes) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  uint64_t key = ((uint64_t)dev << 48) ^ (uint64_t)(uintptr_t)func;
+  std::lock_guard<std::mutex> lk(g_mu);
+  auto it = g_smem_attr.find(key);
+  if (it != g_smem_attr.end() && it->second >= bytes) return cudaSuccess;
+  e = cudaFuncSetAttribute(func, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+  if (e == cudaSuccess) g_smem_attr[key] = bytes;
+  return e;
+}
+
+// cuTensorMapEncodeTiled through the runtime's driver entry point (no -lcuda).
+static PFN_cuTensorMapEncodeTiled_v12000 get_encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  });
+  return fn;
+}
+
+// 2-D tensor map: dims {inner, outer}, row stride in bytes, box {bi, bo}.
+static b2x_status encode_2d(CUtensorMap* m, CUtensorMapDataType dt, const void* base, uint64_t inner, uint64_t outer,
+                            uint64_t row_stride_bytes, uint32_t bi, uint32_t bo, CUtensorMapSwizzle sw,
+                            const char* what) {
+  auto fn = get_encode_fn();
+  if (!fn) return fail(B2X_ERR_CUDA, "cuTensorMapEncodeTiled is not available from the driver");
+  cuuint64_t dims[2] = {inner, outer};
+  cuuint64_t strides[1] = {row_stride_bytes};
+  cuuint32_t box[2] = {bi, bo};
+  cuuint32_t es[2] = {1, 1};
+  CUresult r = fn(m, dt, 2, const_cast<void*>(base), dims, strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE, sw,
+                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS)
+    return fail(B2X_ERR_INVALID_ARG, "cuTensorMapEncodeTiled(%s) failed with %d (dims %llu x %llu, stride %llu)",
+                what, (int)r, (unsigned long long)inner, (unsigned long long)outer,
+                (unsigned long long)row_stride_bytes);
+  return B2X_OK;
+}
+
+static bool is_fp8(b2x_dtype t) { return t == B2X_E4M3 || t == B2X_E5M2; }
+static uint64_t align_up(uint64_t x, uint64_t a) { return (x + a - 1) / a * a; }
+
+}  // namespace b2x
+
+using namespace b2x;
+
+extern "C" {
+
+const char* b2x_last_error(void) { return t_err; }
+int b2x_abi_version(void) { return B2X_ABI_VERSION; }
+uint64_t b2x_launch_count(void) { return g_launches.load(); }
+
+b2x_status b2x_read_device_status(int* status_out) {
+  int v = 0, zero = 0;
+  cudaError_t e = cudaMemcpyFromSymbol(&v, g_status, sizeof(int));
+  if (e != cudaSuccess) return cuda_fail(e, "reading the device status word");
+  e = cudaMemcpyToSymbol(g_status, &zero, sizeof(int));
+  if (e != cudaSuccess) return cuda_fail(e, "clearing the device status word");
+  if (status_out) *status_out = v;
+  return B2X_OK;
+}
+
+// ---------------------------------------------------------------------- cast
+
+static int64_t cast_nsegs(const b2x_cast_args* a) {
+  bool flat = a->ld_x == a->cols && a->ld_q == a->cols;
+  int64_t cols = flat ? a->rows * a->cols : a->cols;
+  int64_t rows = flat ? 1 : a->rows;
+  return rows * ((cols + 127) / 128);
+}
+
+size_t b2x_cast_workspace_size(const b2x_cast_args* a) {
+  if (!a || a->mode != B2X_SCALE_TENSOR) return 0;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  return (size_t)cast_num_partials(cast_nsegs(a), device_num_sms(dev)) * sizeof(uint32_t);
+}
+
+b2x_status b2x_fp8_cast(const b2x_cast_args* a, void* stream) {
+  t_err[0] = 0;
+  if (!a) return fail(B2X_ERR_INVALID_ARG, "b2x_fp8_cast: args is NULL");
+  if (a->x_type != B2X_F32 && a->x_type != B2X_BF16)
+    return fail(B2X_ERR_UNSUPPORTED, "b2x_fp8_cast: input dtype must be fp32 or bf16 (got %d)", (int)a->x_type);
+  if (!is_fp8(a->q_type))
+    return fail(B2X_ERR_UNSUPPORTED, "b2x_fp8_cast: output dtype must be e4m3 or e5m2 (got %d)", (int)a->q_type);
+  if (a->rows < 0 || a->cols < 0) return fail(B2X_ERR_INVALID_ARG, "b2x_fp8_cast: negative shape");
+  if (a->rows == 0 || a->cols == 0) return B2X_OK;
+  if (!a->x || !a->q) return fail(B2X_ERR_INVALID_ARG, "b2x_fp8_cast: NULL x or q");
+  if (a->ld_x < a->cols || a->ld_q < a->cols)
+    return fail(B2X_ERR_INVALID_ARG, "b2x_fp8_cast: row stride smaller than cols");
+  if (a->mode != B2X_SCALE_NONE && !a->scale) return fail(B2X_ERR_INVALID_ARG, "b2x_fp8_cast: NULL scale");
+  int64_t sc_cols = 0;
+  switch (a->mode) {
+    case B2X_SCALE_NONE:
+    case B2X_SCALE_TENSOR:
+    case B2X_SCALE_TENSOR_GIVEN:
+      break;
+    case B2X_SCALE_BLOCK_1x128:
+      sc_cols = (a->cols + 127) / 128;
+      break;
+    case B2X_SCALE_MX_1x32:
+      sc_cols = (a->cols + 31) / 32;
+      break;
+    case B2X_SCALE_BLOCK_128x128:
+      sc_cols = (a->cols + 127) / 128;
+      break;
+    default:
+      return fail(B2X_ERR_INVALID_ARG, "b2x_fp8_cast: unknown scale mode %d", (int)a->mode);
+  }
+  if (sc_cols && a->ld_scale < sc_cols)
+    return fail(B2X_ERR_INVALID_ARG, "b2x_fp8_cast: ld_scale %lld < %lld scale columns", (long long)a->ld_scale,
+                (long long)sc_cols);
+  if (a->mode == B2X_SCALE_TENSOR) {
+    size_t need = b2x_cast_workspace_size(a);
+    if (!a->workspace || a->workspace_bytes < need)
+      return fail(B2X_ERR_WORKSPACE, "b2x_fp8_cast: per-tensor amax needs a %zu-byte workspace (got %zu)", need,
+                  a->workspace_bytes);
+  }
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+  e = launch_cast(*a, device_num_sms(dev), (cudaStream_t)stream);
+  if (e != cudaSuccess) return cuda_fail(e, "b2x_fp8_cast launch");
+  return B2X_OK;
+}
+
+b2x_status b2x_amax(const void* x, b2x_dtype xt, int64_t rows, int64_t cols, int64_t ld_x, float* out,
+                    void* workspace, size_t workspace_bytes, void* stream) {
+  t_err[0] = 0;
+  if (xt != B2X_F32 && xt != B2X_BF16) return fail(B2X_ERR_UNSUPPORTED, "b2x_amax: dtype must be fp32 or bf16");
+  if (!x || !out || rows <= 0 || cols <= 0 || ld_x < cols) return fail(B2X_ERR_INVALID_ARG, "b2x_amax: bad args");
+  b2x_cast_args tmp{};
+  tmp.rows = rows;
+  tmp.cols = cols;
+  tmp.ld_x = ld_x;
+  tmp.ld_q = ld_x;
+  tmp.mode = B2X_SCALE_TENSOR;
+  size_t need = b2x_cast_workspace_size(&tmp);
+  if (!workspace || workspace_bytes < need)
+    return fail(B2X_ERR_WORKSPACE, "b2x_amax: needs a %zu-byte workspace (got %zu)", need, workspace_bytes);
+  int dev = 0;
+  cudaGetDevice(&dev);
+  cudaError_t e =
+      launch_amax(x, xt, rows, cols, ld_x, out, (uint32_t*)workspace, device_num_sms(dev), (cudaStream_t)stream);
+  if (e != cudaSuccess) return cuda_fail(e, "b2x_amax launch");
+  return B2X_OK;
+}
+
+// ---------------------------------------------------------------------- GEMM
+
+static int ceil_div(int64_t a, int64_t b) { return (int)((a + b - 1) / b); }
+
+b2x_status b2x_gemm_default_config(const b2x_gemm_args* a, b2x_gemm_config* out) {
+  t_err[0] = 0;
+  if (!a || !out) return fail(B2X_ERR_INVALID_ARG, "b2x_gemm_default_config: NULL argument");
+  int dev = 0;
+  cudaGetDevice(&dev);
+  const int sms = device_num_sms(dev);
+  b2x_gemm_config c = a->config;
+  const bool b_mn = a->ldb_n == 1 && a->ldb_k != 1;
+  const bool blockscaled = a->scale_mode == B2X_SCALE_BLOCK_1x128;
+  c.block_m = 128;
+  c.block_k = 128;
+  if (blockscaled) {
+    c.block_n = 128;  // B scales are per 128x128 tile: one scale per N tile and K block
+    c.split_k = 1;
+  }
+  if (c.block_n == 0) {
+    // Prefer 256-wide tiles (lower shared-memory read traffic per MMA); take
+    // 128 when it clearly fills the last wave better.
+    double best = -1;
+    int cands[2] = {256, 128};
+    for (int bn : cands) {
+      int64_t units = (int64_t)ceil_div(a->M, 128) * ceil_div(a->N, bn);
+      int64_t waves = (units + sms - 1) / sms;
+      double eff = (double)units / (double)(waves * sms) * (bn == 256 ? 1.0 : 0.93);
+      if (eff > best + 1e-9) best = eff, c.block_n = bn;
+    }
+    if (a->N <= 64 && !b_mn) c.block_n = 64;
+  }
+  const int k_tiles = ceil_div(a->K, 128);
+  if (c.split_k == 0) {
+    // Split-K only when the output tiles cannot fill the GPU, each split
+    // keeps >= 4 K blocks (the gating of preprocess_configs :487-497).
+    c.split_k = 1;
+    int64_t mn = (int64_t)ceil_div(a->M, 128) * ceil_div(a->N, c.block_n);
+    if (mn < sms && (a->N % 4) == 0) {
+      // Also try narrower tiles: decode shapes are bandwidth-bound and want
+      // many small units to spread the B stream over all SMs.
+      int best_bn = c.block_n, best_sk = 1;
+      double best_eff = 0;
+      int bns[3] = {c.block_n, 128, 64};
+      for (int bn : bns) {
+        if (b_mn && bn < 128) continue;
+        if (a->config.block_n && bn != a->config.block_n) continue;
+        int64_t mnb = (int64_t)ceil_div(a->M, 128) * ceil_div(a->N, bn);
+        for (int sk = 1; sk <= 16; ++sk) {
+          if (k_tiles < sk || k_tiles / sk < 4) break;
+          int kps = ceil_div(k_tiles, sk);
+          if ((int64_t)(sk - 1) * kps >= k_tiles) continue;  // every split owns >= 1 block
+          int64_t units = mnb * sk;
+          int64_t waves = (units + sms - 1) / sms;
+          double eff = (double)units / (double)(waves * sms);
+          double fill = units >= sms ? 1.0 : (double)units / sms;
+          double score = eff * fill;
+          if (score > best_eff + 1e-6) best_eff = score, best_bn = bn, best_sk = sk;
+        }
+      }
+      c.block_n = best_bn;
+      c.split_k = best_sk;
+    }
+  }
+  if (c.group_size_m == 0) {
+    // _select_group_size_m (blackwell_gemm_ws.py:344-368) in units of 128-row tiles.
+    int num_m_tiles = ceil_div(a->M, 128);
+    double ratio = (double)a->M / (double)(a->N > 0 ? a->N : 1);
+    if (ratio > 10)
+      c.group_size_m = 1;
+    else if (ratio < 0.1)
+      c.group_size_m = num_m_tiles < 64 ? num_m_tiles : 64;
+    else
+      c.group_size_m = num_m_tiles < 8 ? num_m_tiles : 8;
+    if (c.group_size_m < 1) c.group_size_m = 1;
+  }
+  if (c.num_tmem_buffers == 0) c.num_tmem_buffers = 2;
+  if (c.num_mma_groups == 0) c.num_mma_groups = 1;
+  if (c.epilogue_subtile == 0) c.epilogue_subtile = c.block_n / 64 > 0 ? c.block_n / 64 : 1;
+  if (c.num_ctas == 0) c.num_ctas = 1;
+  *out = c;
+  return B2X_OK;
+}
+
+size_t b2x_gemm_workspace_size(const b2x_gemm_args* a) {
+  if (!a) return 0;
+  b2x_gemm_config c;
+  if (b2x_gemm_default_config(a, &c) != B2X_OK) return 0;
+  if (c.split_k <= 1) return 0;
+  uint64_t tiles = (uint64_t)ceil_div(a->M, 128) * ceil_div(a->N, c.block_n);
+  return (size_t)(align_up((uint64_t)a->M * a->N * 4, 256) + align_up(tiles * 4, 256));
+}
+
+b2x_status b2x_fp8_gemm(const b2x_gemm_args* a, void* stream) {
+  t_err[0] = 0;
+  if (!a) return fail(B2X_ERR_INVALID_ARG, "b2x_fp8_gemm: args is NULL");
+  if (!is_fp8(a->a_type) || !is_fp8(a->b_type))
+    return fail(B2X_ERR_UNSUPPORTED, "b2x_fp8_gemm: A and B must be e4m3 or e5m2 (got %d, %d)", (int)a->a_type,
+                (int)a->b_type);
+  if (a->c_type != B2X_BF16 && a->c_type != B2X_F16)
+    return fail(B2X_ERR_UNSUPPORTED, "b2x_fp8_gemm: C must be bf16 or fp16 (got %d)", (int)a->c_type);
+  if (a->M < 0 || a->N < 0 || a->K < 0) return fail(B2X_ERR_INVALID_ARG, "b2x_fp8_gemm: negative shape");
+  if (a->M == 0 || a->N == 0) return B2X_OK;
+  if (a->K == 0) return fail(B2X_ERR_UNSUPPORTED, "b2x_fp8_gemm: K == 0 (C would be all zero)");
+  if (a->M >= (1LL << 31) || a->N >= (1LL << 31) || a->K >= (1LL << 31))
+    return fail(B2X_ERR_UNSUPPORTED, "b2x_fp8_gemm: dimensions must be < 2^31");
+  if (!a->a || !a->b || !a->c) return fail(B2X_ERR_INVALID_ARG, "b2x_fp8_gemm: NULL A, B or C");
+  if (a->lda < a->K) return fail(B2X_ERR_INVALID_ARG, "b2x_fp8_gemm: lda (%lld) < K (%lld)", (long long)a->lda,
+                                 (long long)a->K);
+  if ((a->lda % 16) || ((uintptr_t)a->a % 16))
+    return fail(B2X_ERR_INVALID_ARG, "b2x_fp8_gemm: A must be 16-byte aligned with lda %% 16 == 0");
+  bool b_mn;
+  if (a->ldb_k == 1 && a->ldb_n >= a->K) {
+    b_mn = false;
+    if ((a->ldb_n % 16) || ((uintptr_t)a->b % 16))
+      return fail(B2X_ERR_INVALID_ARG, "b2x_fp8_gemm: K-major B needs 16-byte alignment and a row stride %% 16 == 0");
+  } else if (a->ldb_n == 1 && a->ldb_k >= a->N) {
+    b_mn = true;
+    if ((a->ldb_k % 16) || ((uintptr_t)a->b % 16))
+      return fail(B2X_ERR_INVALID_ARG, "b2x_fp8_gemm: row-major B needs 16-byte alignment and a row stride %% 16 == 0");
+  } else {
+    return fail(B2X_ERR_INVALID_ARG, "b2x_fp8_gemm: B strides (%lld, %lld) are not K-major or row-major",
+                (long long)a->ldb_k, (long long)a->ldb_n);
+  }
+  if (a->ldc < a->N || (a->ldc % 8) || ((uintptr_t)a->c % 16))
+    return fail(B2X_ERR_INVALID_ARG, "b2x_fp8_gemm: C must be 16-byte aligned with ldc >= N and ldc %% 8 == 0");
+  const bool blockscaled = a->scale_mode == B2X_SCALE_BLOCK_1x128;
+  switch (a->scale_mode) {
+    case B2X_SCALE_NONE:
+      break;
+    case B2X_SCALE_TENSOR:
+    case B2X_SCALE_TENSOR_GIVEN:
+      if (!a->scale_a || !a->scale_b) return fail(B2X_ERR_INVALID_ARG, "b2x_fp8_gemm: NULL scale pointer");
+      break;
+    case B2X_SCALE_BLOCK_1x128:
+      if (!a->scale_a || !a->scale_b) return fail(B2X_ERR_INVALID_ARG, "b2x_fp8_gemm: NULL scale pointer");
+      if (b_mn) return fail(B2X_ERR_UNSUPPORTED, "b2x_fp8_gemm: block-scaled GEMM needs a K-major B");
+      break;
+    default:
+      return fail(B2X_ERR_UNSUPPORTED, "b2x_fp8_gemm: scale mode %d not supported for GEMM", (int)a->scale_mode);
+  }
+
+  b2x_gemm_config c;
+  b2x_status s = b2x_gemm_default_config(a, &c);
+  if (s != B2X_OK) return s;
+  if (c.block_n != 64 && c.block_n != 128 && c.block_n != 256)
+    return fail(B2X_ERR_UNSUPPORTED, "b2x_fp8_gemm: BLOCK_SIZE_N must be 64, 128 or 256 (got %d)", c.block_n);
+  if (b_mn && c.block_n < 128)
+    return fail(B2X_ERR_UNSUPPORTED, "b2x_fp8_gemm: row-major B needs BLOCK_SIZE_N >= 128");
+  if (blockscaled && (c.block_n != 128 || c.split_k > 1))
+    return fail(B2X_ERR_UNSUPPORTED, "b2x_fp8_gemm: block-scaled GEMM runs with BLOCK_SIZE_N = 128, SPLIT_K = 1");
+  const int k_tiles = ceil_div(a->K, 128);
+  if (c.split_k < 1) return fail(B2X_ERR_INVALID_ARG, "b2x_fp8_gemm: SPLIT_K must be >= 1");
+  if (c.split_k > 1) {
+    int kps = ceil_div(k_tiles, c.split_k);
+    if ((int64_t)(c.split_k - 1) * kps >= k_tiles)
+      return fail(B2X_ERR_INVALID_ARG,
+                  "b2x_fp8_gemm: SPLIT_K=%d leaves an empty split for %d K blocks of 128", c.split_k, k_tiles);
+    if (a->N % 4) return fail(B2X_ERR_UNSUPPORTED, "b2x_fp8_gemm: split-K needs N %% 4 == 0");
+    size_t need = b2x_gemm_workspace_size(a);
+    if (!a->workspace || a->workspace_bytes < need || ((uintptr_t)a->workspace % 16))
+      return fail(B2X_ERR_WORKSPACE, "b2x_fp8_gemm: split-K needs a zeroed %zu-byte workspace (got %zu)", need,
+                  a->workspace_bytes);
+  }
+
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+  GemmLaunch g;
+  memset(&g, 0, sizeof(g));
+  g.M = a->M;
+  g.N = a->N;
+  g.K = a->K;
+  g.bn = c.block_n;
+  g.stages = c.num_smem_buffers;
+  g.group_size_m = c.group_size_m;
+  g.split_k = c.split_k;
+  g.a_fmt = a->a_type == B2X_E4M3 ? 0 : 1;
+  g.b_fmt = a->b_type == B2X_E4M3 ? 0 : 1;
+  g.b_mn = b_mn ? 1 : 0;
+  g.c_half = a->c_type == B2X_F16 ? 1 : 0;
+  g.scale_mode = a->scale_mode;
+  g.scale_a = a->scale_a;
+  g.scale_b = a->scale_b;
+  g.sa_stride_m = a->sa_stride_m;
+  g.sa_stride_k = a->sa_stride_k;
+  g.sb_stride_k = a->sb_stride_k;
+  g.sb_stride_n = a->sb_stride_n;
+  g.c = a->c;
+  g.ldc = a->ldc;
+  g.num_sms = device_num_sms(dev);
+  if (c.split_k > 1) {
+    g.ws = reinterpret_cast<float*>(a->workspace);
+    g.counters = reinterpret_cast<int*>(reinterpret_cast<uint8_t*>(a->workspace) +
+                                        align_up((uint64_t)a->M * a->N * 4, 256));
+  }
+
+  s = encode_2d(&g.tmA, CU_TENSOR_MAP_DATA_TYPE_UINT8, a->a, (uint64_t)a->K, (uint64_t)a->M, (uint64_t)a->lda, 128,
+                128, CU_TENSOR_MAP_SWIZZLE_128B, "A");
+  if (s != B2X_OK) return s;
+  if (b_mn)
+    s = encode_2d(&g.tmB, CU_TENSOR_MAP_DATA_TYPE_UINT8, a->b, (uint64_t)a->N, (uint64_t)a->K, (uint64_t)a->ldb_k,
+                  128, 128, CU_TENSOR_MAP_SWIZZLE_128B, "B (row-major)");
+  else
+    s = encode_2d(&g.tmB, CU_TENSOR_MAP_DATA_TYPE_UINT8, a->b, (uint64_t)a->K, (uint64_t)a->N, (uint64_t)a->ldb_n,
+                  128, (uint32_t)c.block_n, CU_TENSOR_MAP_SWIZZLE_128B, "B (K-major)");
+  if (s != B2X_OK) return s;
+  s = encode_2d(&g.tmC, a->c_type == B2X_F16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16,
+                a->c, (uint64_t)a->N, (uint64_t)a->M, (uint64_t)a->ldc * 2, 64, 128, CU_TENSOR_MAP_SWIZZLE_128B, "C");
+  if (s != B2X_OK) return s;
+
+  e = blockscaled ? launch_fp8_gemm_blockscaled(g, (cudaStream_t)stream) : launch_fp8_gemm(g, (cudaStream_t)stream);
+  if (e != cudaSuccess) return cuda_fail(e, "b2x_fp8_gemm launch");
+  return B2X_OK;
+}
+
+b2x_status b2x_splitk_reduce(const void* ws, b2x_dtype wt, void* c, b2x_dtype ct, int64_t M, int64_t N, int64_t ldc,
+                             int split_k, void* stream) {
+  t_err[0] = 0;
+  if (!ws || !c) return fail(B2X_ERR_INVALID_ARG, "b2x_splitk_reduce: NULL pointer");
+  if (M < 0 || N < 0 || split_k < 1 || ldc < N) return fail(B2X_ERR_INVALID_ARG, "b2x_splitk_reduce: bad shape");
+  auto ok_t = [](b2x_dtype t) { return t == B2X_F32 || t == B2X_BF16 || t == B2X_F16; };
+  if (!ok_t(wt) || !ok_t(ct)) return fail(B2X_ERR_UNSUPPORTED, "b2x_splitk_reduce: dtypes must be fp32/bf16/fp16");
+  if (M == 0 || N == 0) return B2X_OK;
+  cudaError_t e = launch_splitk_reduce(ws, wt, c, ct, M, N, ldc, split_k, (cudaStream_t)stream);
+  if (e != cudaSuccess) return cuda_fail(e, "b2x_splitk_reduce launch");
+  return B2X_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,48 @@
+// Internal declarations shared by the b2x host code and kernel launchers.
+#pragma once
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <cstdint>
+#include "b2x.h"
+
+namespace b2x {
+
+// Opt-in shared memory per CTA on sm_100 is 232448 bytes; keep 1 KB for the
+// kernels' static shared variables.
+constexpr int kMaxDynSmem = 232448 - 1024;
+
+// Counts kernel launches (reported through b2x_launch_count()).
+void note_launch(int n);
+
+// Sets cudaFuncAttributeMaxDynamicSharedMemorySize once per (device, kernel).
+cudaError_t ensure_smem_attr(const void* func, int bytes);
+
+cudaError_t launch_cast(const b2x_cast_args& a, int num_sms, cudaStream_t st);
+int cast_num_partials(int64_t nsegs, int num_sms);
+cudaError_t launch_amax(const void* x, b2x_dtype xt, int64_t rows, int64_t cols, int64_t ld_x, float* out,
+                        uint32_t* partials, int num_sms, cudaStream_t st);
+
+struct GemmLaunch {
+  CUtensorMap tmA, tmB, tmC;
+  int64_t M, N, K;
+  int bn, stages, group_size_m, split_k;
+  int a_fmt, b_fmt;  // 0 = e4m3, 1 = e5m2
+  int b_mn;          // B stored row-major [K, N]
+  int c_half;        // fp16 output instead of bf16
+  int scale_mode;
+  const float* scale_a;
+  const float* scale_b;
+  int64_t sa_stride_m, sa_stride_k, sb_stride_k, sb_stride_n;
+  float* ws;
+  int* counters;
+  void* c;
+  int64_t ldc;
+  int num_sms;
+};
+
+cudaError_t launch_fp8_gemm(const GemmLaunch& g, cudaStream_t st);
+cudaError_t launch_fp8_gemm_blockscaled(const GemmLaunch& g, cudaStream_t st);
+cudaError_t launch_splitk_reduce(const void* ws, b2x_dtype wt, void* c, b2x_dtype ct, int64_t M, int64_t N,
+                                 int64_t ldc, int split_k, cudaStream_t st);
+
+}  // namespace b2x

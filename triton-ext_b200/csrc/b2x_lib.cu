@@ -1,0 +1,7 @@
+// Single translation unit for libb2x.so: the device status word and the
+// kernels share one module without relocatable device code.
+#include "b2x_api.cu"
+#include "fp8_cast.cu"
+#include "fp8_gemm.cu"
+#include "fp8_gemm_blockscaled.cu"
+#include "splitk_reduce.cu"

@@ -1,0 +1,428 @@
+// Warp-specialized persistent fp8 GEMM for sm_100a (tcgen05 + TMEM + TMA).
+//
+// Native re-design of matmul_kernel_tma_ws_blackwell
+// (extensions/utlx/tlx/tutorials/blackwell_gemm_ws.py:1089-1349):
+//   producer warp  (:1293-1349, _process_tile_producer_inner :943-1022)
+//       TMA loads of the A and B K-blocks into a ring of STAGES smem buffers;
+//   MMA warp       (:1233-1291, _process_tile_mma_inner :828-939)
+//       one thread issues tcgen05.mma kind::f8f6f4 into a TMEM accumulator,
+//       tcgen05.commit releases each smem stage and, per tile, signals the
+//       accumulator full;
+//   epilogue       (:1180-1231, _process_tile_epilogue_inner :673-824)
+//       two warpgroups ping-pong over two TMEM accumulators (tile i is drained
+//       by warpgroup i%2 while the MMA warp fills the other buffer), scale by
+//       sA*sB, convert, and TMA-store through a 128B-swizzled staging tile --
+//       or, for split-K, reduce fp32 partials with red.global.add.v4.f32.
+// The tile order is the reference's grouped order (_compute_pid :433-439) over
+// a persistent grid (tile_id += gridDim.x), and a split-K unit covers
+// k_tiles_per_split = cdiv(k_tiles, SPLIT_K) K-blocks (:1258-1264).
+//
+// Thread layout (384 threads): warp 0 producer, warp 1 MMA, warp 2 TMEM
+// allocator, warp 3 spare, warps 4-7 epilogue warpgroup 0, warps 8-11
+// epilogue warpgroup 1.  BLOCK_M = 128 (one tcgen05 M=128 group), BLOCK_K =
+// 128 (one 128-byte swizzle row of fp8), BLOCK_N in {64, 128, 256}.
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cstdint>
+#include "b2x_ptx.cuh"
+#include "b2x_internal.h"
+#include "fp8_gemm_common.cuh"
+
+namespace b2x {
+
+template <int BN, int STAGES>
+struct SmemLayout {
+  static constexpr int kABytes = kBM * kBK;        // 16 KB
+  static constexpr int kBBytes = BN * kBK;         // BN x 128 B
+  static constexpr int kStageBytes = kABytes + kBBytes;
+  static constexpr int kCBytes = kBM * 128;        // one 128 x 128 B staging tile per epilogue warpgroup
+  static constexpr int kAOff = 0;
+  static constexpr int kBOff = STAGES * kABytes;
+  static constexpr int kCOff = kBOff + STAGES * kBBytes;
+  static constexpr int kBarOff = kCOff + 2 * kCBytes;
+  // barriers: full[STAGES], empty[STAGES], tfull[2], tempty[2], mma_done, + tmem slot + flags
+  static constexpr int kBarBytes = (2 * STAGES + 5) * 8 + 16;
+  static constexpr int kTotal = kBarOff + kBarBytes;
+  static constexpr int kAlloc = kTotal + 1024;  // slack to align the base to 1024 B
+};
+
+template <int BN>
+struct TmemCols {
+  static constexpr uint32_t kPerBuf = BN;
+  static constexpr uint32_t kAlloc = 2 * BN < 32 ? 32 : 2 * BN;
+};
+
+template <int BN, int STAGES, int B_MN, int SPLITK>
+__global__ void __launch_bounds__(kThreads, 1)
+    fp8_gemm_ws_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                       const __grid_constant__ CUtensorMap tmC, const GemmParams p) {
+  using L = SmemLayout<BN, STAGES>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + L::kBarOff);
+  uint64_t* empty = full + STAGES;
+  uint64_t* tfull = empty + STAGES;
+  uint64_t* tempty = tfull + 2;
+  uint64_t* mma_done = tempty + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(mma_done + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&tfull[b], 1);
+      mbar_init(&tempty[b], 128);
+    }
+    mbar_init(mma_done, 1);
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmB);
+    if (!SPLITK) tma_prefetch_desc(&tmC);
+  }
+  if (warp == 2) {
+    tmem_alloc(tmem_slot, TmemCols<BN>::kAlloc);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+  const int num_pid_in_group = p.group_size_m * p.num_pid_n;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer
+    if (lane == 0) {
+      const uint64_t pol_a = policy_evict_last();
+      const uint64_t pol_b = policy_evict_last();
+      int stage = 0;
+      uint32_t phase = 0;
+      uint32_t issued_mask = 0;
+      uint32_t pend_phase[STAGES > 0 ? STAGES : 1];
+      bool ok = true;
+      for (int unit = blockIdx.x; unit < p.num_units && ok; unit += gridDim.x) {
+        const int mn = unit % p.num_mn_tiles;
+        const int split = unit / p.num_mn_tiles;
+        int pid_m, pid_n;
+        compute_pid(mn, num_pid_in_group, p.num_pid_m, p.group_size_m, pid_m, pid_n);
+        const int k0 = split * p.k_tiles_per_split;
+        const int k1 = min(k0 + p.k_tiles_per_split, p.k_tiles);
+        for (int kb = k0; kb < k1; ++kb) {
+          if (!mbar_wait(&empty[stage], phase ^ 1, abort_flag, kStatusTimeoutProducer)) {
+            ok = false;
+            break;
+          }
+          uint8_t* sA = smem + L::kAOff + stage * L::kABytes;
+          uint8_t* sB = smem + L::kBOff + stage * L::kBBytes;
+          mbar_arrive_expect_tx(&full[stage], L::kStageBytes);
+          tma_load_2d(sA, &tmA, &full[stage], kb * kBK, pid_m * kBM, pol_a);
+          if (B_MN) {
+            // B row-major [K, N]: slabs of 128 N-columns x 128 K-rows.
+#pragma unroll
+            for (int j = 0; j < (BN + 127) / 128; ++j)
+              tma_load_2d(sB + j * 128 * kBK, &tmB, &full[stage], pid_n * BN + j * 128, kb * kBK, pol_b);
+          } else {
+            tma_load_2d(sB, &tmB, &full[stage], kb * kBK, pid_n * BN, pol_b);
+          }
+          issued_mask |= 1u << stage;
+          pend_phase[stage] = phase;
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+      }
+      // Never leave the CTA with TMA writes into its shared memory in flight.
+      for (int s = 0; s < STAGES; ++s)
+        if (issued_mask & (1u << s)) {
+          volatile int no_abort = 0;
+          mbar_wait(&full[s], pend_phase[s], &no_abort, kStatusTimeoutProducer);
+        }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      int local = 0;
+      bool ok = true;
+      for (int unit = blockIdx.x; unit < p.num_units && ok; unit += gridDim.x, ++local) {
+        const int split = unit / p.num_mn_tiles;
+        const int k0 = split * p.k_tiles_per_split;
+        const int k1 = min(k0 + p.k_tiles_per_split, p.k_tiles);
+        const int buf = local & 1;
+        const uint32_t use = (uint32_t)(local >> 1);
+        if (!mbar_wait(&tempty[buf], (use & 1) ^ 1, abort_flag, kStatusTimeoutMma)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + buf * TmemCols<BN>::kPerBuf;
+        for (int kb = k0; kb < k1; ++kb) {
+          if (!mbar_wait(&full[stage], phase, abort_flag, kStatusTimeoutMma)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a_addr = smem_u32(smem + L::kAOff + stage * L::kABytes);
+          const uint32_t b_addr = smem_u32(smem + L::kBOff + stage * L::kBBytes);
+#pragma unroll
+          for (int k = 0; k < kBK / 32; ++k) {
+            const uint64_t adesc = smem_desc_sw128(a_addr + k * 32, 16, 1024);
+            const uint64_t bdesc = B_MN ? smem_desc_sw128(b_addr + k * 32 * 128, 128 * kBK, 1024)
+                                        : smem_desc_sw128(b_addr + k * 32, 16, 1024);
+            mma_f8f6f4(d_tmem, adesc, bdesc, p.idesc, (kb > k0 || k > 0) ? 1u : 0u);
+          }
+          mma_commit(&empty[stage]);
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+        if (!ok) break;
+        mma_commit(&tfull[buf]);
+      }
+      // All MMAs of this thread must finish before TMEM is released.
+      mma_commit(mma_done);
+      volatile int no_abort = 0;
+      mbar_wait(mma_done, 0, &no_abort, kStatusTimeoutMma);
+    }
+  } else if (warp >= kEpiWarp0) {
+    // ------------------------------------------------------------ epilogue
+    const int e = (warp - kEpiWarp0) >> 2;   // warpgroup 0 / 1
+    const int q = warp & 3;                  // TMEM lane quarter of this warp
+    const int row = q * 32 + lane;           // accumulator row held by this thread
+    const uint32_t bar_id = 1 + e;
+    const int wg_tid = threadIdx.x - (kEpiWarp0 + 4 * e) * 32;
+    uint8_t* stage_c = smem + L::kCOff + e * L::kCBytes;
+    float alpha = 1.0f;
+    if (p.scale_mode != B2X_SCALE_NONE) alpha = __fmul_rn(__ldg(p.scale_a), __ldg(p.scale_b));
+    int local = 0;
+    for (int unit = blockIdx.x; unit < p.num_units; unit += gridDim.x, ++local) {
+      if ((local & 1) != e) continue;
+      const int mn = unit % p.num_mn_tiles;
+      int pid_m, pid_n;
+      compute_pid(mn, num_pid_in_group, p.num_pid_m, p.group_size_m, pid_m, pid_n);
+      const uint32_t use = (uint32_t)(local >> 1);
+      bool ok = mbar_wait(&tfull[e], use & 1, abort_flag, kStatusTimeoutEpilogue);
+      if (!wg_all(ok, bar_id)) break;
+      tc_fence_after();
+      const uint32_t t_row = tmem_base + e * TmemCols<BN>::kPerBuf + ((uint32_t)(q * 32) << 16);
+      const int m0 = pid_m * kBM, n0 = pid_n * BN;
+      const int grow = m0 + row;
+
+      if (!SPLITK) {
+#pragma unroll 1
+        for (int c0 = 0; c0 < BN; c0 += 64) {
+          uint32_t v[64];
+          tmem_ld_32x32b_x32(t_row + c0, *reinterpret_cast<uint32_t(*)[32]>(&v[0]));
+          tmem_ld_32x32b_x32(t_row + c0 + 32, *reinterpret_cast<uint32_t(*)[32]>(&v[32]));
+          tmem_ld_wait();
+          uint32_t pk[32];
+#pragma unroll
+          for (int i = 0; i < 32; ++i) {
+            float lo = __fmul_rn(__uint_as_float(v[2 * i]), alpha);
+            float hi = __fmul_rn(__uint_as_float(v[2 * i + 1]), alpha);
+            if (p.c_half) {
+              __half2 h = __floats2half2_rn(lo, hi);
+              pk[i] = *reinterpret_cast<uint32_t*>(&h);
+            } else {
+              pk[i] = pack_bf16x2(lo, hi);
+            }
+          }
+          // The staging tile may still be read by the previous TMA store.
+          if (wg_tid == 0) bulk_wait_group_read0();
+          named_bar_sync(bar_id, 128);
+          uint8_t* srow = stage_c + row * 128;
+#pragma unroll
+          for (int j = 0; j < 8; ++j) {
+            uint4 val = make_uint4(pk[4 * j], pk[4 * j + 1], pk[4 * j + 2], pk[4 * j + 3]);
+            *reinterpret_cast<uint4*>(srow + ((j ^ (row & 7)) << 4)) = val;
+          }
+          fence_proxy_async_smem();
+          named_bar_sync(bar_id, 128);
+          if (wg_tid == 0) {
+            tma_store_2d(&tmC, stage_c, n0 + c0, m0);
+            bulk_commit_group();
+          }
+        }
+        tc_fence_before();
+        mbar_arrive(&tempty[e]);
+      } else {
+        // Split-K: reduce this unit's fp32 partial into the workspace.
+        const bool row_ok = grow < p.M;
+#pragma unroll 1
+        for (int c0 = 0; c0 < BN; c0 += 32) {
+          uint32_t v[32];
+          tmem_ld_32x32b_x32(t_row + c0, v);
+          tmem_ld_wait();
+          if (row_ok) {
+            float* dst = p.ws + (int64_t)grow * p.N + n0 + c0;
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+              const int col = n0 + c0 + 4 * j;
+              if (col + 3 < p.N) {
+                red_add_v4(dst + 4 * j, __uint_as_float(v[4 * j]), __uint_as_float(v[4 * j + 1]),
+                           __uint_as_float(v[4 * j + 2]), __uint_as_float(v[4 * j + 3]));
+              } else {
+                for (int t = 0; t < 4; ++t)
+                  if (col + t < p.N) atomicAdd(dst + 4 * j + t, __uint_as_float(v[4 * j + t]));
+              }
+            }
+          }
+        }
+        tc_fence_before();
+        mbar_arrive(&tempty[e]);
+        // Last unit to arrive on this tile converts the sum and re-zeroes the
+        // workspace so the next call finds it clean.
+        __threadfence();
+        named_bar_sync(bar_id, 128);
+        __shared__ int s_last[2];
+        if (wg_tid == 0) {
+          int old = atomicAdd(p.counters + mn, 1);
+          s_last[e] = (old == p.split_k - 1);
+        }
+        named_bar_sync(bar_id, 128);
+        if (s_last[e]) {
+          __threadfence();
+          if (row_ok) {
+            float* src = p.ws + (int64_t)grow * p.N + n0;
+            uint8_t* crow = reinterpret_cast<uint8_t*>(p.c) + ((int64_t)grow * p.ldc + n0) * 2;
+            for (int c = 0; c < BN; c += 8) {
+              if (n0 + c >= p.N) break;
+              float f[8];
+              if (n0 + c + 7 < p.N) {
+                float4 x0 = __ldcg(reinterpret_cast<const float4*>(src + c));
+                float4 x1 = __ldcg(reinterpret_cast<const float4*>(src + c + 4));
+                f[0] = x0.x; f[1] = x0.y; f[2] = x0.z; f[3] = x0.w;
+                f[4] = x1.x; f[5] = x1.y; f[6] = x1.z; f[7] = x1.w;
+                __stcg(reinterpret_cast<float4*>(src + c), make_float4(0.f, 0.f, 0.f, 0.f));
+                __stcg(reinterpret_cast<float4*>(src + c + 4), make_float4(0.f, 0.f, 0.f, 0.f));
+                uint32_t pk[4];
+#pragma unroll
+                for (int i = 0; i < 4; ++i) {
+                  float lo = __fmul_rn(f[2 * i], alpha), hi = __fmul_rn(f[2 * i + 1], alpha);
+                  if (p.c_half) {
+                    __half2 h = __floats2half2_rn(lo, hi);
+                    pk[i] = *reinterpret_cast<uint32_t*>(&h);
+                  } else {
+                    pk[i] = pack_bf16x2(lo, hi);
+                  }
+                }
+                if (((p.ldc & 7) == 0) && ((reinterpret_cast<uintptr_t>(p.c) & 15) == 0))
+                  *reinterpret_cast<uint4*>(crow + c * 2) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+                else
+                  for (int i = 0; i < 4; ++i) {
+                    reinterpret_cast<uint16_t*>(crow)[c + 2 * i] = (uint16_t)(pk[i] & 0xFFFF);
+                    reinterpret_cast<uint16_t*>(crow)[c + 2 * i + 1] = (uint16_t)(pk[i] >> 16);
+                  }
+              } else {
+                for (int t = 0; t < 8 && n0 + c + t < p.N; ++t) {
+                  float s = __ldcg(src + c + t);
+                  src[c + t] = 0.f;
+                  float o = __fmul_rn(s, alpha);
+                  uint16_t h = p.c_half ? __half_as_ushort(__float2half_rn(o))
+                                        : __bfloat16_as_ushort(__float2bfloat16_rn(o));
+                  reinterpret_cast<uint16_t*>(crow)[c + t] = h;
+                }
+              }
+            }
+          }
+          if (wg_tid == 0) p.counters[mn] = 0;
+        }
+      }
+    }
+    if (!SPLITK && wg_tid == 0) bulk_wait_group0();
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 2) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, TmemCols<BN>::kAlloc);
+  }
+}
+
+// ----------------------------------------------------------------------------
+// Host launch.
+
+template <int BN, int STAGES, int B_MN, int SPLITK>
+static cudaError_t launch_gemm_t(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tc,
+                                 const GemmParams& p, int grid, cudaStream_t st) {
+  using L = SmemLayout<BN, STAGES>;
+  auto kern = fp8_gemm_ws_kernel<BN, STAGES, B_MN, SPLITK>;
+  cudaError_t e = ensure_smem_attr(reinterpret_cast<const void*>(kern), L::kAlloc);
+  if (e != cudaSuccess) return e;
+  kern<<<grid, kThreads, L::kAlloc, st>>>(ta, tb, tc, p);
+  note_launch(1);
+  return cudaGetLastError();
+}
+
+template <int BN, int B_MN, int SPLITK>
+static cudaError_t dispatch_stages(int stages, const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tc,
+                                   const GemmParams& p, int grid, cudaStream_t st) {
+  // Largest ring that fits next to the two epilogue staging tiles.
+  constexpr int kMaxStages = (kMaxDynSmem - 2 * kBM * 128 - 1024 - 256) / (kBM * kBK + BN * kBK);
+  constexpr int kS = kMaxStages > 8 ? 8 : kMaxStages;
+  if (stages <= 0 || stages > kS) stages = kS;
+  switch (stages) {
+    case 2: return launch_gemm_t<BN, 2, B_MN, SPLITK>(ta, tb, tc, p, grid, st);
+    case 3: return launch_gemm_t<BN, (kS >= 3 ? 3 : 2), B_MN, SPLITK>(ta, tb, tc, p, grid, st);
+    case 4: return launch_gemm_t<BN, (kS >= 4 ? 4 : 2), B_MN, SPLITK>(ta, tb, tc, p, grid, st);
+    case 5: return launch_gemm_t<BN, (kS >= 5 ? 5 : 2), B_MN, SPLITK>(ta, tb, tc, p, grid, st);
+    case 6: return launch_gemm_t<BN, (kS >= 6 ? 6 : 2), B_MN, SPLITK>(ta, tb, tc, p, grid, st);
+    default: return launch_gemm_t<BN, kS, B_MN, SPLITK>(ta, tb, tc, p, grid, st);
+  }
+}
+
+template <int B_MN, int SPLITK>
+static cudaError_t dispatch_bn(int bn, int stages, const CUtensorMap& ta, const CUtensorMap& tb,
+                               const CUtensorMap& tc, const GemmParams& p, int grid, cudaStream_t st) {
+  switch (bn) {
+    case 256: return dispatch_stages<256, B_MN, SPLITK>(stages, ta, tb, tc, p, grid, st);
+    case 128: return dispatch_stages<128, B_MN, SPLITK>(stages, ta, tb, tc, p, grid, st);
+    case 64: return dispatch_stages<64, B_MN, SPLITK>(stages, ta, tb, tc, p, grid, st);
+    default: return cudaErrorInvalidValue;
+  }
+}
+
+cudaError_t launch_fp8_gemm(const GemmLaunch& g, cudaStream_t st) {
+  GemmParams p{};
+  p.M = (int)g.M;
+  p.N = (int)g.N;
+  p.K = (int)g.K;
+  p.num_pid_m = (int)((g.M + kBM - 1) / kBM);
+  p.num_pid_n = (int)((g.N + g.bn - 1) / g.bn);
+  p.num_mn_tiles = p.num_pid_m * p.num_pid_n;
+  p.split_k = g.split_k;
+  p.num_units = p.num_mn_tiles * g.split_k;
+  p.group_size_m = g.group_size_m;
+  p.k_tiles = (int)((g.K + kBK - 1) / kBK);
+  p.k_tiles_per_split = (p.k_tiles + g.split_k - 1) / g.split_k;
+  p.idesc = idesc_f8f6f4(g.a_fmt, g.b_fmt, 0, g.b_mn ? 1 : 0, kBM, g.bn);
+  p.c_half = g.c_half;
+  p.scale_mode = g.scale_mode;
+  p.scale_a = g.scale_a;
+  p.scale_b = g.scale_b;
+  p.ws = g.ws;
+  p.counters = g.counters;
+  p.c = g.c;
+  p.ldc = g.ldc;
+  int grid = p.num_units < g.num_sms ? p.num_units : g.num_sms;
+  if (g.split_k > 1) {
+    return g.b_mn ? dispatch_bn<1, 1>(g.bn, g.stages, g.tmA, g.tmB, g.tmC, p, grid, st)
+                  : dispatch_bn<0, 1>(g.bn, g.stages, g.tmA, g.tmB, g.tmC, p, grid, st);
+  }
+  return g.b_mn ? dispatch_bn<1, 0>(g.bn, g.stages, g.tmA, g.tmB, g.tmC, p, grid, st)
+                : dispatch_bn<0, 0>(g.bn, g.stages, g.tmA, g.tmB, g.tmC, p, grid, st);
+}
+
+}  // namespace b2x
