@@ -1,0 +1,193 @@
+"""CPU tests of the C ABI boundary: libb2x.so loads, exports every symbol that
+include/b2x.h declares, and rejects bad requests with status codes and
+messages before touching a GPU.  No kernel is launched here."""
+import ctypes
+import os
+import re
+
+import pytest
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+HEADER = os.path.join(ROOT, "include", "b2x.h")
+
+
+def _lib():
+    from b2x import _lib as L
+    return L
+
+
+def declared_symbols():
+    text = open(HEADER).read()
+    return sorted(set(re.findall(r"B2X_API\s+[\w\s\*]+?\b(b2x_\w+)\s*\(", text)))
+
+
+def test_header_declares_the_boundary():
+    syms = declared_symbols()
+    for s in ("b2x_fp8_gemm", "b2x_fp8_cast", "b2x_splitk_reduce", "b2x_gemm_workspace_size",
+              "b2x_cast_workspace_size", "b2x_last_error"):
+        assert s in syms
+
+
+def test_library_exports_every_declared_symbol():
+    L = _lib()
+    lib = ctypes.CDLL(L.LIB_PATH)
+    missing = [s for s in declared_symbols() if not hasattr(lib, s)]
+    assert not missing, f"declared in b2x.h but not exported: {missing}"
+    assert set(declared_symbols()) == set(L.EXPORTED)
+
+
+def test_abi_version_matches_header():
+    L = _lib()
+    v = int(re.search(r"#define B2X_ABI_VERSION (\d+)", open(HEADER).read()).group(1))
+    assert L.lib().b2x_abi_version() == v
+
+
+def test_struct_layouts_match_header():
+    """The ctypes mirrors of the ABI structs have the C sizes."""
+    import shutil
+    import subprocess
+    import tempfile
+    L = _lib()
+    cc = shutil.which("gcc") or shutil.which("cc")
+    if cc is None:
+        pytest.skip("no C compiler")
+    src = '#include <stdio.h>\n#include "b2x.h"\nint main(){printf("%zu %zu %zu\\n", sizeof(b2x_cast_args),' \
+          ' sizeof(b2x_gemm_config), sizeof(b2x_gemm_args)); return 0;}\n'
+    with tempfile.TemporaryDirectory() as d:
+        with open(os.path.join(d, "p.c"), "w") as f:
+            f.write(src)
+        exe = os.path.join(d, "p")
+        subprocess.run([cc, "-I", os.path.join(ROOT, "include"), os.path.join(d, "p.c"), "-o", exe], check=True)
+        sizes = [int(v) for v in subprocess.run([exe], capture_output=True, text=True, check=True).stdout.split()]
+    assert sizes == [ctypes.sizeof(L.CastArgs), ctypes.sizeof(L.GemmConfig), ctypes.sizeof(L.GemmArgs)]
+
+
+def _gemm_args(**kw):
+    L = _lib()
+    g = L.GemmArgs()
+    g.a, g.b, g.c = 0x10000, 0x20000, 0x30000
+    g.M, g.N, g.K = 256, 256, 256
+    g.lda, g.ldb_k, g.ldb_n, g.ldc = 256, 1, 256, 256
+    g.a_type = g.b_type = L.E4M3
+    g.c_type = L.BF16
+    g.scale_mode = L.SCALE_NONE
+    for k, v in kw.items():
+        setattr(g, k, v)
+    return g
+
+
+@pytest.mark.parametrize("field,value,status", [
+    ("a_type", 1, "ERR_UNSUPPORTED"),          # bf16 A: not this library's path
+    ("c_type", 3, "ERR_UNSUPPORTED"),          # fp8 C
+    ("lda", 200, "ERR_INVALID_ARG"),           # lda < K
+    ("lda", 264, "ERR_INVALID_ARG"),           # lda % 16 != 0
+    ("a", 0, "ERR_INVALID_ARG"),               # NULL A
+    ("a", 0x10008, "ERR_INVALID_ARG"),         # misaligned A
+    ("ldb_k", 3, "ERR_INVALID_ARG"),           # neither K-major nor row-major
+    ("ldc", 100, "ERR_INVALID_ARG"),           # ldc < N
+    ("K", 0, "ERR_UNSUPPORTED"),
+    ("M", -1, "ERR_INVALID_ARG"),
+])
+def test_gemm_rejects_bad_arguments(field, value, status):
+    L = _lib()
+    g = _gemm_args(**{field: value})
+    st = L.lib().b2x_fp8_gemm(ctypes.byref(g), None)
+    assert st == getattr(L, status), L.lib().b2x_last_error()
+    assert L.lib().b2x_last_error()
+
+
+def test_gemm_split_k_needs_workspace():
+    L = _lib()
+    g = _gemm_args()
+    g.config.split_k = 2
+    assert L.lib().b2x_gemm_workspace_size(ctypes.byref(g)) == 256 * 256 * 4 + 256
+    assert L.lib().b2x_fp8_gemm(ctypes.byref(g), None) == L.ERR_WORKSPACE
+    g.config.split_k = 3  # 2 K blocks of 128 cannot feed 3 splits
+    assert L.lib().b2x_fp8_gemm(ctypes.byref(g), None) == L.ERR_INVALID_ARG
+
+
+def test_gemm_zero_sized_is_a_no_op():
+    L = _lib()
+    g = _gemm_args(M=0)
+    assert L.lib().b2x_fp8_gemm(ctypes.byref(g), None) == L.OK
+
+
+def test_block_scaled_requires_kmajor_b():
+    L = _lib()
+    g = _gemm_args(ldb_k=256, ldb_n=1, scale_mode=L.SCALE_BLOCK_1x128, scale_a=0x40000, scale_b=0x50000)
+    assert L.lib().b2x_fp8_gemm(ctypes.byref(g), None) == L.ERR_UNSUPPORTED
+
+
+def _cast_args(**kw):
+    L = _lib()
+    a = L.CastArgs()
+    a.x, a.x_type, a.rows, a.cols, a.ld_x = 0x10000, L.F32, 64, 256, 256
+    a.q, a.q_type, a.ld_q = 0x20000, L.E4M3, 256
+    a.scale, a.mode, a.ld_scale = 0x30000, L.SCALE_BLOCK_1x128, 2
+    for k, v in kw.items():
+        setattr(a, k, v)
+    return a
+
+
+@pytest.mark.parametrize("field,value,status", [
+    ("x_type", 2, "ERR_UNSUPPORTED"),   # fp16 input
+    ("q_type", 1, "ERR_UNSUPPORTED"),   # bf16 output
+    ("x", 0, "ERR_INVALID_ARG"),
+    ("ld_x", 100, "ERR_INVALID_ARG"),
+    ("ld_scale", 1, "ERR_INVALID_ARG"),
+    ("mode", 42, "ERR_INVALID_ARG"),
+    ("scale", 0, "ERR_INVALID_ARG"),
+])
+def test_cast_rejects_bad_arguments(field, value, status):
+    L = _lib()
+    a = _cast_args(**{field: value})
+    assert L.lib().b2x_fp8_cast(ctypes.byref(a), None) == getattr(L, status)
+
+
+def test_cast_per_tensor_needs_workspace():
+    L = _lib()
+    a = _cast_args(mode=L.SCALE_TENSOR)
+    assert L.lib().b2x_cast_workspace_size(ctypes.byref(a)) > 0
+    assert L.lib().b2x_fp8_cast(ctypes.byref(a), None) == L.ERR_WORKSPACE
+
+
+def test_splitk_reduce_rejects_bad_arguments():
+    L = _lib()
+    lib = L.lib()
+    assert lib.b2x_splitk_reduce(None, L.F32, 0x1000, L.BF16, 4, 4, 4, 2, None) == L.ERR_INVALID_ARG
+    assert lib.b2x_splitk_reduce(0x1000, L.E4M3, 0x2000, L.BF16, 4, 4, 4, 2, None) == L.ERR_UNSUPPORTED
+    assert lib.b2x_splitk_reduce(0x1000, L.F32, 0x2000, L.BF16, 4, 4, 2, 2, None) == L.ERR_INVALID_ARG
+
+
+def _default_config(M, N, K, kmajor=True, **cfg):
+    L = _lib()
+    g = _gemm_args(M=M, N=N, K=K, lda=K, ldc=N)
+    if kmajor:
+        g.ldb_k, g.ldb_n = 1, K
+    else:
+        g.ldb_k, g.ldb_n = N, 1
+    for k, v in cfg.items():
+        setattr(g.config, k, v)
+    out = L.GemmConfig()
+    assert L.lib().b2x_gemm_default_config(ctypes.byref(g), ctypes.byref(out)) == L.OK
+    return out
+
+
+def test_default_config_large_square_uses_wide_tiles_no_split():
+    c = _default_config(8192, 8192, 8192)
+    assert (c.block_m, c.block_n, c.block_k, c.split_k) == (128, 256, 128, 1)
+    assert c.group_size_m == 8
+
+
+def test_default_config_decode_uses_split_k():
+    c = _default_config(64, 8192, 28672)
+    assert c.split_k > 1
+    assert (28672 // 128) // c.split_k >= 4
+    assert c.group_size_m == 1  # one M tile
+
+
+def test_default_config_keeps_caller_fields():
+    c = _default_config(64, 8192, 28672, split_k=8, block_n=128)
+    assert (c.split_k, c.block_n) == (8, 128)
+    c = _default_config(4096, 4096, 4096, kmajor=False)
+    assert c.block_n >= 128  # row-major B is streamed in 128-column slabs

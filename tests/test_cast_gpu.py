@@ -113,18 +113,21 @@ def test_cast_full_size_64M(src, mode):
     for fmt in (O.E4M3, O.E5M2):
         fm = float(O.FMAX[fmt])
         q, s = b2x.quantize(x, mode, FP8[fmt])
+        # fp32 divisions / products evaluated in float64 and rounded once to
+        # float32 are the IEEE-rounded fp32 results (torch's tensor/scalar
+        # division multiplies by a reciprocal, which is not).
         xf = x.float()
-        absx = torch.nan_to_num(xf.abs(), nan=0.0)
+        absx = torch.where(torch.isnan(xf), torch.zeros_like(xf), xf.abs())
         if mode == "tensor":
-            sc = (absx.max() / fm).reshape(1, 1)
+            sc = (absx.max().double() / fm).float().reshape(1, 1)
         else:
-            sc = (absx.reshape(R, C // 128, 128).amax(-1) / fm)
+            sc = (absx.reshape(R, C // 128, 128).amax(-1).double() / fm).float()
         assert torch.equal(s.reshape(sc.shape).view(torch.int32), sc.view(torch.int32))
-        inv = torch.where(sc == 0, torch.zeros_like(sc), 1.0 / sc)
+        inv = torch.where(sc == 0, torch.zeros_like(sc), (1.0 / sc.double()).float())
         if mode == "tensor":
-            y = xf * inv
+            y = (xf.double() * inv.double()).float()
         else:
-            y = (xf.reshape(R, C // 128, 128) * inv[..., None]).reshape(R, C)
+            y = (xf.reshape(R, C // 128, 128).double() * inv[..., None].double()).float().reshape(R, C)
         y = torch.where(torch.isnan(y), torch.full_like(y, fm), y.clamp(-fm, fm))  # scaled: NaN -> +FMAX
         ref = y.to(FP8[fmt]).view(torch.uint8)
         got = q.view(torch.uint8)

@@ -108,8 +108,9 @@ def test_splitk_matches_oracle_and_nonsplit(split_k, b_layout):
         _check(cs, ref, ad, bd, f"split_k={split_k} rep={rep}")
         _check(cs, c1.astype(np.float64), ad, bd, "split vs non-split")
     from b2x import ops
-    for buf in ops._ws_cache.values():
-        assert int(buf.count_nonzero().item()) == 0, "split-K workspace not left zeroed"
+    for key, buf in ops._ws_cache.items():
+        if key[2]:  # the zero-invariant split-K workspaces (not the amax partials)
+            assert int(buf.count_nonzero().item()) == 0, "split-K workspace not left zeroed"
 
 
 def test_splitk_decode_shape_full():

@@ -106,7 +106,7 @@ def quantize_op(x: torch.Tensor, mode: str, fp8_dtype: torch.dtype,
     if mode == "given":
         if scale is None:
             raise ValueError("mode 'given' needs a scale tensor")
-        sc = scale.to(torch.float32).reshape(1).contiguous()
+        sc = scale.to(torch.float32).reshape(1).clone()  # a custom op may not return an alias of an input
     else:
         sc = torch.empty(sshape, dtype=sdt, device=x.device)
     a = L.CastArgs()
