@@ -189,6 +189,22 @@ B2X_API b2x_status b2x_fp8_gemm(const b2x_gemm_args* args, void* stream);
 B2X_API b2x_status b2x_splitk_reduce(const void* ws, b2x_dtype ws_type, void* c, b2x_dtype c_type, int64_t M, int64_t N,
                              int64_t ldc, int split_k, void* stream);
 
+/*
+ * Same GEMM as b2x_fp8_gemm, for callers that cannot allocate device memory
+ * (a serving loop that reserves all memory up front, a plugin running inside
+ * another framework's memory pool, a host with no allocator behind its C
+ * interface).  It takes no workspace: split-K partial sums go to a scratch
+ * array built into the library (8 MiB per device, held until the process
+ * exits), so M*N*4 must stay below about 8 MiB; larger split-K problems are
+ * rejected with B2X_ERR_WORKSPACE.  It calls no allocator.  All calls on a
+ * device share the scratch: each call clears what it uses first, and calls
+ * that overlap on the GPU (unordered streams) race.  The first call on a
+ * device looks up the scratch address; make it before any stream capture.
+ * No counterpart in the reference (which always allocates its split-K
+ * workspace with torch.empty).
+ */
+B2X_API b2x_status b2x_fp8_gemm_splitk_noalloc(const b2x_gemm_args* args, void* stream);
+
 /* ------------------------------------------------------------------ misc */
 
 /* Message for the calling thread's last failed call ("" if none). */

@@ -5,3 +5,4 @@
 #include "fp8_gemm.cu"
 #include "fp8_gemm_blockscaled.cu"
 #include "splitk_reduce.cu"
+#include "fp8_gemm_noalloc.cu"
