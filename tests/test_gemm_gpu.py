@@ -113,6 +113,26 @@ def test_splitk_matches_oracle_and_nonsplit(split_k, b_layout):
             assert int(buf.count_nonzero().item()) == 0, "split-K workspace not left zeroed"
 
 
+@pytest.mark.parametrize("shape", [(256, 256, 256), (384, 520, 1024), (129, 1000, 640), (1000, 256, 4096)])
+@pytest.mark.parametrize("b_layout", ["kmajor", "rowmajor"])
+def test_paired_cta_matches_single_cta_and_oracle(shape, b_layout):
+    """NUM_CTAS=2 (cta_group::2 256x256 tiles over two SMs) against NUM_CTAS=1 and the oracle."""
+    M, N, K = shape
+    a, sa = _quant((M, K), O.E4M3, 21)
+    b, sb = _quant((K, N), O.E4M3, 22)
+    ref = O.gemm(a, b, scale_mode="tensor", scale_a=sa, scale_b=sb)
+    ad, bd = O.fp8_bits_to_f64(a, O.E4M3) * sa, O.fp8_bits_to_f64(b, O.E4M3) * sb
+    c2 = _gemm(a, b, O.E4M3, O.E4M3, sa, sb, b_layout, config={"NUM_CTAS": 2, "BLOCK_SIZE_N": 256})
+    c1 = _gemm(a, b, O.E4M3, O.E4M3, sa, sb, b_layout, config={"NUM_CTAS": 1, "BLOCK_SIZE_N": 256})
+    _check(c2, ref, ad, bd, f"pair {shape} {b_layout}")
+    _check(c1, ref, ad, bd, f"single {shape} {b_layout}")
+    assert b2x_status_ok()
+
+
+def b2x_status_ok():
+    return _b2x().read_device_status() == 0
+
+
 def test_splitk_decode_shape_full():
     """BASELINE config: M=64 N=8192 K=28672, SPLIT_K=8, per-tensor e4m3, bf16 out.
     Checked against the oracle on a sample of 512 output columns."""

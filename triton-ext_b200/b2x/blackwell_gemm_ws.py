@@ -278,7 +278,7 @@ def _to_b2x_config(cfg: dict, K: int) -> list:
         warnings.warn(f"SPLIT_K={cfg.get('SPLIT_K')} leaves empty splits over {k_tiles} K blocks of 128; "
                       f"using SPLIT_K={sk}", stacklevel=3)
     return [128, bn, 128, group, 0, int(cfg.get("NUM_TMEM_BUFFERS", 2)), int(cfg.get("NUM_MMA_GROUPS", 1)),
-            int(cfg.get("EPILOGUE_SUBTILE", 1)), int(cfg.get("NUM_CTAS", 1)), sk,
+            int(cfg.get("EPILOGUE_SUBTILE", 1)), int(cfg.get("NUM_CTAS", 0)), sk,
             int(cfg.get("INTERLEAVE_EPILOGUE", 0))]
 
 

@@ -287,7 +287,12 @@ b2x_status b2x_gemm_default_config(const b2x_gemm_args* a, b2x_gemm_config* out)
   if (c.num_tmem_buffers == 0) c.num_tmem_buffers = 2;
   if (c.num_mma_groups == 0) c.num_mma_groups = 1;
   if (c.epilogue_subtile == 0) c.epilogue_subtile = c.block_n / 64 > 0 ? c.block_n / 64 : 1;
-  if (c.num_ctas == 0) c.num_ctas = 1;
+  // Paired CTAs (256x256 tiles over two SMs) for large non-split problems:
+  // a third less operand traffic per SM.  Needs 256-wide tiles and more
+  // than one 128-row block of M.
+  const bool pair_ok = c.split_k == 1 && c.block_n == 256 && !blockscaled && a->M > 128;
+  if (c.num_ctas == 0) c.num_ctas = pair_ok ? 2 : 1;
+  if (c.num_ctas == 2 && !pair_ok) c.num_ctas = 1;
   *out = c;
   return B2X_OK;
 }
@@ -399,6 +404,7 @@ b2x_status b2x_fp8_gemm(const b2x_gemm_args* a, void* stream) {
   g.c = a->c;
   g.ldc = a->ldc;
   g.num_sms = device_num_sms(dev);
+  g.pair = c.num_ctas == 2 ? 1 : 0;
   if (c.split_k > 1) {
     g.ws = reinterpret_cast<float*>(a->workspace);
     g.counters = reinterpret_cast<int*>(reinterpret_cast<uint8_t*>(a->workspace) +
@@ -413,13 +419,18 @@ b2x_status b2x_fp8_gemm(const b2x_gemm_args* a, void* stream) {
                   128, 128, CU_TENSOR_MAP_SWIZZLE_128B, "B (row-major)");
   else
     s = encode_2d(&g.tmB, CU_TENSOR_MAP_DATA_TYPE_UINT8, a->b, (uint64_t)a->K, (uint64_t)a->N, (uint64_t)a->ldb_n,
-                  128, (uint32_t)c.block_n, CU_TENSOR_MAP_SWIZZLE_128B, "B (K-major)");
+                  128, g.pair ? 128u : (uint32_t)c.block_n, CU_TENSOR_MAP_SWIZZLE_128B, "B (K-major)");
   if (s != B2X_OK) return s;
   s = encode_2d(&g.tmC, a->c_type == B2X_F16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16,
                 a->c, (uint64_t)a->N, (uint64_t)a->M, (uint64_t)a->ldc * 2, 64, 128, CU_TENSOR_MAP_SWIZZLE_128B, "C");
   if (s != B2X_OK) return s;
 
-  e = blockscaled ? launch_fp8_gemm_blockscaled(g, (cudaStream_t)stream) : launch_fp8_gemm(g, (cudaStream_t)stream);
+  if (blockscaled)
+    e = launch_fp8_gemm_blockscaled(g, (cudaStream_t)stream);
+  else if (g.pair)
+    e = launch_fp8_gemm_pair(g, (cudaStream_t)stream);
+  else
+    e = launch_fp8_gemm(g, (cudaStream_t)stream);
   if (e != cudaSuccess) return cuda_fail(e, "b2x_fp8_gemm launch");
   return B2X_OK;
 }

@@ -38,9 +38,11 @@ struct GemmLaunch {
   void* c;
   int64_t ldc;
   int num_sms;
+  int pair;          // paired-CTA (cta_group::2) 256x256 tiles
 };
 
 cudaError_t launch_fp8_gemm(const GemmLaunch& g, cudaStream_t st);
+cudaError_t launch_fp8_gemm_pair(const GemmLaunch& g, cudaStream_t st);
 cudaError_t launch_fp8_gemm_blockscaled(const GemmLaunch& g, cudaStream_t st);
 cudaError_t launch_splitk_reduce(const void* ws, b2x_dtype wt, void* c, b2x_dtype ct, int64_t M, int64_t N,
                                  int64_t ldc, int split_k, cudaStream_t st);

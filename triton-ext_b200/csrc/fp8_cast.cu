@@ -9,12 +9,15 @@
 //   q     = rne_satfinite_fp8(clamp(x * inv, -FMAX, FMAX))     (:72-84)
 // with IEEE-rounded divisions and a single (non-fused) multiply.
 //
-// Work decomposition: a "segment" is 128 consecutive columns of one row; one
-// warp owns a segment at a time and each lane holds 4 consecutive elements
-// (16 B of fp32 / 8 B of bf16 per load, 4 B of fp8 per store, so a warp moves
-// fully coalesced 512 B / 256 B in and 128 B out).  Segments are unrolled
-// SEGS_PER_ITER deep per warp to keep enough bytes in flight for HBM3e.
+// Work decomposition: a "segment" is 256 consecutive columns of one row; one
+// warp owns a segment at a time and each lane holds 8 consecutive elements
+// (32 B of fp32 or 16 B of bf16 per lane, 8 B of fp8 out), so every access
+// is a full 16-byte vector and a warp moves fully coalesced 1 KB / 512 B in
+// and 256 B out.  Segments are unrolled per warp and the grid is sized from
+// the occupancy calculator so all CTAs are resident at once (one wave) with
+// enough bytes in flight for HBM3e.
 #include <cuda_bf16.h>
+#include <algorithm>
 #include <cstdint>
 #include "b2x_ptx.cuh"
 #include "b2x_internal.h"
@@ -47,7 +50,7 @@ __device__ __forceinline__ uint16_t cvt2(float lo, float hi) {
 // a plain-Triton restatement of the recipe).
 __device__ __forceinline__ float clamp_sym(float y, float m) { return copysignf(fminf(fabsf(y), m), y); }
 
-// Quantize 4 values.  SCALED: multiply by inv first; the GPU's fp32 multiply
+// Quantize values.  SCALED: multiply by inv first; the GPU's fp32 multiply
 // returns the canonical (positive) NaN for any NaN result, so after scaling
 // every NaN -- including Inf * 0 -- saturates to +FMAX.  Unscaled (mode NONE,
 // where the recipe has no multiply) a NaN keeps its sign.
@@ -64,53 +67,67 @@ __device__ __forceinline__ uint32_t quant4(float4 v, float inv) {
   return (uint32_t)cvt2<FP8>(a, b) | ((uint32_t)cvt2<FP8>(c, d) << 16);
 }
 
-__device__ __forceinline__ float nan_ignoring_absmax(float m, float v) { return fmaxf(m, fabsf(v)); }
-__device__ __forceinline__ float absmax4(float4 v) {
-  return fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w)));
-}
-
 __device__ __forceinline__ float bf16_bits_to_f32(uint16_t b) { return __uint_as_float((uint32_t)b << 16); }
+__device__ __forceinline__ float bf16lo(uint32_t u) { return __uint_as_float(u << 16); }
+__device__ __forceinline__ float bf16hi(uint32_t u) { return __uint_as_float(u & 0xFFFF0000u); }
 
-// Load 4 consecutive elements starting at column `col` of a row; elements at
-// or beyond `cols` read as 0.  `vec_ok` says the row base is aligned so a
-// full 4-wide vector load is legal.
+constexpr int kSeg = 256;  // columns per warp step
+constexpr int kLaneElems = 8;
+
+// Load 8 consecutive elements from column `col` of a row; elements at or
+// beyond `cols` read as 0.  `vec_ok`: the row base is 16-byte aligned.
 template <typename T>
-__device__ __forceinline__ float4 load4(const T* row, int64_t col, int64_t cols, bool vec_ok);
+__device__ __forceinline__ void load8(const T* row, int64_t col, int64_t cols, bool vec_ok, float (&v)[8]);
 
 template <>
-__device__ __forceinline__ float4 load4<float>(const float* row, int64_t col, int64_t cols, bool vec_ok) {
-  if (vec_ok && col + 3 < cols) return __ldcs(reinterpret_cast<const float4*>(row + col));
-  float4 r = make_float4(0.f, 0.f, 0.f, 0.f);
-  if (col + 0 < cols) r.x = row[col + 0];
-  if (col + 1 < cols) r.y = row[col + 1];
-  if (col + 2 < cols) r.z = row[col + 2];
-  if (col + 3 < cols) r.w = row[col + 3];
-  return r;
-}
-
-template <>
-__device__ __forceinline__ float4 load4<uint16_t>(const uint16_t* row, int64_t col, int64_t cols, bool vec_ok) {
-  if (vec_ok && col + 3 < cols) {
-    uint2 u = __ldcs(reinterpret_cast<const uint2*>(row + col));
-    return make_float4(bf16_bits_to_f32(u.x & 0xFFFF), bf16_bits_to_f32(u.x >> 16), bf16_bits_to_f32(u.y & 0xFFFF),
-                       bf16_bits_to_f32(u.y >> 16));
-  }
-  float4 r = make_float4(0.f, 0.f, 0.f, 0.f);
-  if (col + 0 < cols) r.x = bf16_bits_to_f32(row[col + 0]);
-  if (col + 1 < cols) r.y = bf16_bits_to_f32(row[col + 1]);
-  if (col + 2 < cols) r.z = bf16_bits_to_f32(row[col + 2]);
-  if (col + 3 < cols) r.w = bf16_bits_to_f32(row[col + 3]);
-  return r;
-}
-
-__device__ __forceinline__ void store4(uint8_t* row, int64_t col, int64_t cols, bool vec_ok, uint32_t q) {
-  if (vec_ok && col + 3 < cols) {
-    __stcs(reinterpret_cast<uint32_t*>(row + col), q);
+__device__ __forceinline__ void load8<float>(const float* row, int64_t col, int64_t cols, bool vec_ok,
+                                             float (&v)[8]) {
+  if (vec_ok && col + 7 < cols) {
+    float4 a = __ldcs(reinterpret_cast<const float4*>(row + col));
+    float4 b = __ldcs(reinterpret_cast<const float4*>(row + col + 4));
+    v[0] = a.x, v[1] = a.y, v[2] = a.z, v[3] = a.w, v[4] = b.x, v[5] = b.y, v[6] = b.z, v[7] = b.w;
     return;
   }
 #pragma unroll
-  for (int i = 0; i < 4; ++i)
-    if (col + i < cols) row[col + i] = (uint8_t)(q >> (8 * i));
+  for (int i = 0; i < 8; ++i) v[i] = (col + i < cols) ? row[col + i] : 0.f;
+}
+
+template <>
+__device__ __forceinline__ void load8<uint16_t>(const uint16_t* row, int64_t col, int64_t cols, bool vec_ok,
+                                                float (&v)[8]) {
+  if (vec_ok && col + 7 < cols) {
+    uint4 u = __ldcs(reinterpret_cast<const uint4*>(row + col));
+    v[0] = bf16lo(u.x), v[1] = bf16hi(u.x), v[2] = bf16lo(u.y), v[3] = bf16hi(u.y);
+    v[4] = bf16lo(u.z), v[5] = bf16hi(u.z), v[6] = bf16lo(u.w), v[7] = bf16hi(u.w);
+    return;
+  }
+#pragma unroll
+  for (int i = 0; i < 8; ++i) v[i] = (col + i < cols) ? bf16_bits_to_f32(row[col + i]) : 0.f;
+}
+
+__device__ __forceinline__ void store8(uint8_t* row, int64_t col, int64_t cols, bool vec_ok, uint2 q) {
+  if (vec_ok && col + 7 < cols) {
+    __stcs(reinterpret_cast<uint2*>(row + col), q);
+    return;
+  }
+#pragma unroll
+  for (int i = 0; i < 8; ++i)
+    if (col + i < cols) row[col + i] = (uint8_t)((i < 4 ? q.x : q.y) >> (8 * (i & 3)));
+}
+
+template <int FP8, bool SCALED = true>
+__device__ __forceinline__ uint2 quant8(const float (&v)[8], float inv) {
+  uint2 r;
+  r.x = quant4<FP8, SCALED>(make_float4(v[0], v[1], v[2], v[3]), inv);
+  r.y = quant4<FP8, SCALED>(make_float4(v[4], v[5], v[6], v[7]), inv);
+  return r;
+}
+
+__device__ __forceinline__ float absmax8(const float (&v)[8]) {
+  float m = 0.f;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) m = fmaxf(m, fabsf(v[i]));  // fmaxf ignores NaN
+  return m;
 }
 
 struct CastGeom {
@@ -118,44 +135,41 @@ struct CastGeom {
   int64_t rows, cols, ld_x;
   uint8_t* q;
   int64_t ld_q;
-  int64_t segs_per_row;  // ceil(cols / 128)
+  int64_t segs_per_row;  // ceil(cols / 256)
   int64_t nsegs;         // rows * segs_per_row
-  bool x_vec, q_vec;     // vector loads / stores legal
+  bool x_vec, q_vec;     // 16-byte loads / 8-byte stores legal
 };
 
-template <int SEGS>
-struct SegBatch {
-  int64_t row[SEGS];
-  int64_t col[SEGS];
-  bool valid[SEGS];
-};
+// Row and first column of this lane in segment s.
+__device__ __forceinline__ void seg_pos(const CastGeom& g, int64_t s, int lane, int64_t& r, int64_t& c) {
+  r = g.segs_per_row == 1 ? s : s / g.segs_per_row;
+  c = (s - r * g.segs_per_row) * kSeg + lane * kLaneElems;
+}
 
 // ----------------------------------------------------------------------------
 // Per-tensor amax, pass 1: each CTA writes the NaN-ignoring max |x| of its
-// share into partials[blockIdx.x] (as fp32 bits; values are >= 0 so the bit
-// patterns order like the floats).
-template <typename T, int SEGS>
+// share into partials[blockIdx.x] (as fp32 bits).
+template <typename T, int U>
 __global__ void __launch_bounds__(256) amax_partial_kernel(CastGeom g, uint32_t* partials) {
   const int lane = threadIdx.x & 31;
   const int64_t warp = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
   const int64_t nwarps = (int64_t)gridDim.x * (blockDim.x >> 5);
   const T* x = reinterpret_cast<const T*>(g.x);
   float m = 0.f;
-  for (int64_t s0 = warp * SEGS; s0 < g.nsegs; s0 += nwarps * SEGS) {
-    float4 v[SEGS];
+  for (int64_t s0 = warp * U; s0 < g.nsegs; s0 += nwarps * U) {
+    float v[U][8];
 #pragma unroll
-    for (int u = 0; u < SEGS; ++u) {
-      int64_t s = s0 + u;
-      if (s < g.nsegs) {
-        int64_t r = g.segs_per_row == 1 ? s : s / g.segs_per_row;
-        int64_t c = (s - r * g.segs_per_row) * 128 + lane * 4;
-        v[u] = load4<T>(x + r * g.ld_x, c, g.cols, g.x_vec);
-      } else {
-        v[u] = make_float4(0.f, 0.f, 0.f, 0.f);
-      }
+    for (int u = 0; u < U; ++u) {
+      int64_t r, c;
+      seg_pos(g, s0 + u, lane, r, c);
+      if (s0 + u < g.nsegs)
+        load8<T>(x + r * g.ld_x, c, g.cols, g.x_vec, v[u]);
+      else
+#pragma unroll
+        for (int i = 0; i < 8; ++i) v[u][i] = 0.f;
     }
 #pragma unroll
-    for (int u = 0; u < SEGS; ++u) m = fmaxf(m, absmax4(v[u]));
+    for (int u = 0; u < U; ++u) m = fmaxf(m, absmax8(v[u]));
   }
 #pragma unroll
   for (int o = 16; o; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
@@ -197,9 +211,9 @@ __global__ void amax_final_kernel(const uint32_t* partials, int n, float* out) {
 }
 
 // ----------------------------------------------------------------------------
-// Uniform-scale quantize: modes NONE (inv = 1), TENSOR_GIVEN (inv from
+// Uniform-scale quantize: modes NONE (no multiply), TENSOR_GIVEN (inv from
 // scale[0]) and TENSOR (inv from the amax partials; CTA 0 writes scale[0]).
-template <typename T, int FP8, int SEGS>
+template <typename T, int FP8, int U>
 __global__ void __launch_bounds__(256) quant_uniform_kernel(CastGeom g, int mode, float* scale,
                                                             const uint32_t* partials, int npartials) {
   constexpr float FM = Fp8Traits<FP8>::kMax;
@@ -221,111 +235,105 @@ __global__ void __launch_bounds__(256) quant_uniform_kernel(CastGeom g, int mode
   }
   __syncthreads();
   const float inv = s_inv;
+  const bool scaled = mode != B2X_SCALE_NONE;
   const int lane = threadIdx.x & 31;
   const int64_t warp = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
   const int64_t nwarps = (int64_t)gridDim.x * (blockDim.x >> 5);
   const T* x = reinterpret_cast<const T*>(g.x);
-  for (int64_t s0 = warp * SEGS; s0 < g.nsegs; s0 += nwarps * SEGS) {
-    float4 v[SEGS];
-    int64_t rr[SEGS], cc[SEGS];
+  for (int64_t s0 = warp * U; s0 < g.nsegs; s0 += nwarps * U) {
+    float v[U][8];
+    int64_t rr[U], cc[U];
 #pragma unroll
-    for (int u = 0; u < SEGS; ++u) {
-      int64_t s = s0 + u;
-      rr[u] = -1;
-      if (s < g.nsegs) {
-        int64_t r = g.segs_per_row == 1 ? s : s / g.segs_per_row;
-        rr[u] = r;
-        cc[u] = (s - r * g.segs_per_row) * 128 + lane * 4;
-        v[u] = load4<T>(x + r * g.ld_x, cc[u], g.cols, g.x_vec);
-      }
+    for (int u = 0; u < U; ++u) {
+      seg_pos(g, s0 + u, lane, rr[u], cc[u]);
+      if (s0 + u < g.nsegs) load8<T>(x + rr[u] * g.ld_x, cc[u], g.cols, g.x_vec, v[u]);
     }
-    if (mode == B2X_SCALE_NONE) {
 #pragma unroll
-      for (int u = 0; u < SEGS; ++u)
-        if (rr[u] >= 0) store4(g.q + rr[u] * g.ld_q, cc[u], g.cols, g.q_vec, quant4<FP8, false>(v[u], inv));
-    } else {
-#pragma unroll
-      for (int u = 0; u < SEGS; ++u)
-        if (rr[u] >= 0) store4(g.q + rr[u] * g.ld_q, cc[u], g.cols, g.q_vec, quant4<FP8>(v[u], inv));
+    for (int u = 0; u < U; ++u) {
+      if (s0 + u >= g.nsegs) continue;
+      uint2 q = scaled ? quant8<FP8>(v[u], inv) : quant8<FP8, false>(v[u], inv);
+      store8(g.q + rr[u] * g.ld_q, cc[u], g.cols, g.q_vec, q);
     }
   }
 }
 
 // ----------------------------------------------------------------------------
 // Row-block scales: GROUP = 128 (fp32 scale per 1x128) or 32 (E8M0 per 1x32).
-// A warp covers one 128-column segment: 128/GROUP groups of GROUP/4 lanes.
-template <typename T, int FP8, int GROUP, int SEGS>
+// A warp covers one 256-column segment: 256/GROUP groups of GROUP/8 lanes.
+template <typename T, int FP8, int GROUP, int U>
 __global__ void __launch_bounds__(256) quant_rowblock_kernel(CastGeom g, void* scale, int64_t ld_scale) {
   constexpr float FM = Fp8Traits<FP8>::kMax;
-  constexpr int LPG = GROUP / 4;  // lanes per group
+  constexpr int LPG = GROUP / kLaneElems;  // lanes per group
   const int lane = threadIdx.x & 31;
   const int64_t warp = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
   const int64_t nwarps = (int64_t)gridDim.x * (blockDim.x >> 5);
   const T* x = reinterpret_cast<const T*>(g.x);
-  for (int64_t s0 = warp * SEGS; s0 < g.nsegs; s0 += nwarps * SEGS) {
-    float4 v[SEGS];
-    int64_t rr[SEGS], cc[SEGS];
+  for (int64_t s0 = warp * U; s0 < g.nsegs; s0 += nwarps * U) {
+    float v[U][8];
+    int64_t rr[U], cc[U];
 #pragma unroll
-    for (int u = 0; u < SEGS; ++u) {
-      int64_t s = s0 + u;
-      rr[u] = -1;
-      cc[u] = 0;
-      v[u] = make_float4(0.f, 0.f, 0.f, 0.f);
-      if (s < g.nsegs) {
-        int64_t r = g.segs_per_row == 1 ? s : s / g.segs_per_row;
-        rr[u] = r;
-        cc[u] = (s - r * g.segs_per_row) * 128 + lane * 4;
-        v[u] = load4<T>(x + r * g.ld_x, cc[u], g.cols, g.x_vec);
-      }
+    for (int u = 0; u < U; ++u) {
+      seg_pos(g, s0 + u, lane, rr[u], cc[u]);
+      if (s0 + u < g.nsegs)
+        load8<T>(x + rr[u] * g.ld_x, cc[u], g.cols, g.x_vec, v[u]);
+      else
+#pragma unroll
+        for (int i = 0; i < 8; ++i) v[u][i] = 0.f;
     }
 #pragma unroll
-    for (int u = 0; u < SEGS; ++u) {
-      // Lanes of a segment past the end of the tensor take part in the
-      // shuffles (they hold zeros) but store nothing.
-      float m = absmax4(v[u]);
+    for (int u = 0; u < U; ++u) {
+      // Lanes past the end of the row (or of the tensor) take part in the
+      // shuffles holding zeros but store nothing.
+      const bool live = s0 + u < g.nsegs;
+      float m = absmax8(v[u]);
 #pragma unroll
       for (int o = LPG / 2; o; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
       float inv;
+      const bool leader = live && (lane % LPG) == 0 && cc[u] < g.cols;
       if constexpr (GROUP == 32) {
         float descale = __fdiv_rn(m, FM);
         uint32_t e = (__float_as_uint(descale) + 0x007FFFFFu) & 0x7F800000u;
         float rounded = __uint_as_float(e);
         inv = rounded == 0.f ? 0.f : __fdiv_rn(1.0f, rounded);
-        if (rr[u] >= 0 && (lane % LPG) == 0 && cc[u] < g.cols)
-          reinterpret_cast<uint8_t*>(scale)[rr[u] * ld_scale + cc[u] / GROUP] = (uint8_t)(e >> 23);
+        if (leader) reinterpret_cast<uint8_t*>(scale)[rr[u] * ld_scale + cc[u] / GROUP] = (uint8_t)(e >> 23);
       } else {
         float sc = __fdiv_rn(m, FM);
         inv = sc == 0.f ? 0.f : __fdiv_rn(1.0f, sc);
-        if (rr[u] >= 0 && lane == 0 && cc[u] < g.cols)
-          reinterpret_cast<float*>(scale)[rr[u] * ld_scale + cc[u] / GROUP] = sc;
+        if (leader) reinterpret_cast<float*>(scale)[rr[u] * ld_scale + cc[u] / GROUP] = sc;
       }
-      if (rr[u] >= 0) store4(g.q + rr[u] * g.ld_q, cc[u], g.cols, g.q_vec, quant4<FP8>(v[u], inv));
+      if (live) store8(g.q + rr[u] * g.ld_q, cc[u], g.cols, g.q_vec, quant8<FP8>(v[u], inv));
     }
   }
 }
 
 // ----------------------------------------------------------------------------
-// 128x128 tile scales: one CTA of 256 threads (8 warps x 16 rows) per tile,
-// the tile held in registers between the amax and the quantize step.
+// 128x128 tile scales: one CTA of 256 threads per tile.  A warp covers two
+// rows per step (lanes 0-15 one row, 16-31 the next), 16 rows in 8 steps, and
+// keeps them in registers between the amax and the quantize step.
 template <typename T, int FP8>
 __global__ void __launch_bounds__(256) quant_tile128_kernel(CastGeom g, float* scale, int64_t ld_scale,
                                                             int64_t tiles_c, int64_t ntiles) {
   constexpr float FM = Fp8Traits<FP8>::kMax;
   const int lane = threadIdx.x & 31;
   const int w = threadIdx.x >> 5;
+  const int half = lane >> 4;
   const T* x = reinterpret_cast<const T*>(g.x);
   __shared__ float red[8];
   __shared__ float s_inv;
   for (int64_t t = blockIdx.x; t < ntiles; t += gridDim.x) {
     const int64_t tr = t / tiles_c, tc = t - tr * tiles_c;
-    const int64_t c = tc * 128 + lane * 4;
-    float4 v[16];
+    const int64_t c = tc * 128 + (lane & 15) * kLaneElems;
+    float v[8][8];
     float m = 0.f;
 #pragma unroll
-    for (int i = 0; i < 16; ++i) {
-      int64_t r = tr * 128 + w * 16 + i;
-      v[i] = r < g.rows ? load4<T>(x + r * g.ld_x, c, g.cols, g.x_vec) : make_float4(0.f, 0.f, 0.f, 0.f);
-      m = fmaxf(m, absmax4(v[i]));
+    for (int i = 0; i < 8; ++i) {
+      const int64_t r = tr * 128 + w * 16 + 2 * i + half;
+      if (r < g.rows && c < tc * 128 + 128)
+        load8<T>(x + r * g.ld_x, c, g.cols, g.x_vec, v[i]);
+      else
+#pragma unroll
+        for (int j = 0; j < 8; ++j) v[i][j] = 0.f;
+      m = fmaxf(m, absmax8(v[i]));
     }
 #pragma unroll
     for (int o = 16; o; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
@@ -342,9 +350,9 @@ __global__ void __launch_bounds__(256) quant_tile128_kernel(CastGeom g, float* s
     __syncthreads();
     const float inv = s_inv;
 #pragma unroll
-    for (int i = 0; i < 16; ++i) {
-      int64_t r = tr * 128 + w * 16 + i;
-      if (r < g.rows) store4(g.q + r * g.ld_q, c, g.cols, g.q_vec, quant4<FP8>(v[i], inv));
+    for (int i = 0; i < 8; ++i) {
+      const int64_t r = tr * 128 + w * 16 + 2 * i + half;
+      if (r < g.rows) store8(g.q + r * g.ld_q, c, g.cols, g.q_vec, quant8<FP8>(v[i], inv));
     }
     __syncthreads();  // red / s_inv are reused by the next tile
   }
@@ -353,54 +361,71 @@ __global__ void __launch_bounds__(256) quant_tile128_kernel(CastGeom g, float* s
 // ----------------------------------------------------------------------------
 // Host-side launchers (called from b2x_api.cu after argument validation).
 
-static int cast_grid(int64_t nsegs, int segs_per_warp, int num_sms) {
+// CTAs of 256 threads that fit on one SM at once (per kernel, cached).
+template <typename K>
+static int resident_ctas(K kern) {
+  static int n = 0;  // one cache per kernel instantiation
+  if (n == 0) {
+    int v = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&v, kern, 256, 0) != cudaSuccess || v <= 0) v = 4;
+    n = v;
+  }
+  return n;
+}
+
+static int grid_for(int64_t nsegs, int segs_per_warp, int per_sm, int num_sms) {
   int64_t warps_needed = (nsegs + segs_per_warp - 1) / segs_per_warp;
   int64_t blocks = (warps_needed + 7) / 8;
-  int64_t cap = (int64_t)num_sms * 8;  // 8 CTAs of 256 threads per SM fill all 64 warp slots
+  int64_t cap = (int64_t)num_sms * per_sm;  // one full wave
   if (blocks > cap) blocks = cap;
   if (blocks < 1) blocks = 1;
   return (int)blocks;
 }
 
-int cast_num_partials(int64_t nsegs, int num_sms) { return cast_grid(nsegs, 4, num_sms); }
+// Upper bound on the per-tensor amax partials (one per CTA of the amax pass).
+int cast_num_partials(int64_t nsegs, int num_sms) {
+  return grid_for(nsegs, 4, 8, num_sms);
+}
 
 template <typename T, int FP8>
 static cudaError_t launch_cast_t(const CastGeom& g, int mode, void* scale, int64_t ld_scale, uint32_t* partials,
                                  int num_sms, cudaStream_t st) {
-  constexpr int SEGS = sizeof(T) == 4 ? 4 : 8;
+  constexpr int U = sizeof(T) == 4 ? 2 : 4;  // 64 B in flight per lane either way
   switch (mode) {
     case B2X_SCALE_NONE:
-    case B2X_SCALE_TENSOR_GIVEN: {
-      int grid = cast_grid(g.nsegs, SEGS, num_sms);
-      quant_uniform_kernel<T, FP8, SEGS><<<grid, 256, 0, st>>>(g, mode, (float*)scale, nullptr, 0);
+    case B2X_SCALE_TENSOR_GIVEN:
+    case B2X_SCALE_TENSOR: {
+      int np = 0;
+      if (mode == B2X_SCALE_TENSOR) {
+        auto ak = amax_partial_kernel<T, 4>;
+        np = grid_for(g.nsegs, 4, std::min(8, resident_ctas(ak)), num_sms);
+        ak<<<np, 256, 0, st>>>(g, partials);
+        note_launch(1);
+      }
+      auto k = quant_uniform_kernel<T, FP8, U>;
+      int grid = grid_for(g.nsegs, U, resident_ctas(k), num_sms);
+      k<<<grid, 256, 0, st>>>(g, mode, (float*)scale, partials, np);
       note_launch(1);
       break;
     }
-    case B2X_SCALE_TENSOR: {
-      int np = cast_num_partials(g.nsegs, num_sms);
-      amax_partial_kernel<T, 4><<<np, 256, 0, st>>>(g, partials);
-      int grid = cast_grid(g.nsegs, SEGS, num_sms);
-      quant_uniform_kernel<T, FP8, SEGS><<<grid, 256, 0, st>>>(g, mode, (float*)scale, partials, np);
-      note_launch(2);
-      break;
-    }
     case B2X_SCALE_BLOCK_1x128: {
-      int grid = cast_grid(g.nsegs, SEGS, num_sms);
-      quant_rowblock_kernel<T, FP8, 128, SEGS><<<grid, 256, 0, st>>>(g, scale, ld_scale);
+      auto k = quant_rowblock_kernel<T, FP8, 128, U>;
+      k<<<grid_for(g.nsegs, U, resident_ctas(k), num_sms), 256, 0, st>>>(g, scale, ld_scale);
       note_launch(1);
       break;
     }
     case B2X_SCALE_MX_1x32: {
-      int grid = cast_grid(g.nsegs, SEGS, num_sms);
-      quant_rowblock_kernel<T, FP8, 32, SEGS><<<grid, 256, 0, st>>>(g, scale, ld_scale);
+      auto k = quant_rowblock_kernel<T, FP8, 32, U>;
+      k<<<grid_for(g.nsegs, U, resident_ctas(k), num_sms), 256, 0, st>>>(g, scale, ld_scale);
       note_launch(1);
       break;
     }
     case B2X_SCALE_BLOCK_128x128: {
+      auto k = quant_tile128_kernel<T, FP8>;
       int64_t tiles_r = (g.rows + 127) / 128, tiles_c = (g.cols + 127) / 128;
       int64_t nt = tiles_r * tiles_c;
-      int64_t grid = nt < (int64_t)num_sms * 8 ? nt : (int64_t)num_sms * 8;
-      quant_tile128_kernel<T, FP8><<<(int)grid, 256, 0, st>>>(g, (float*)scale, ld_scale, tiles_c, nt);
+      int64_t cap = (int64_t)num_sms * resident_ctas(k);
+      k<<<(int)(nt < cap ? nt : cap), 256, 0, st>>>(g, (float*)scale, ld_scale, tiles_c, nt);
       note_launch(1);
       break;
     }
@@ -410,26 +435,31 @@ static cudaError_t launch_cast_t(const CastGeom& g, int mode, void* scale, int64
   return cudaGetLastError();
 }
 
-cudaError_t launch_cast(const b2x_cast_args& a, int num_sms, cudaStream_t st) {
-  CastGeom g;
-  g.x = a.x;
-  g.rows = a.rows;
-  g.cols = a.cols;
-  g.ld_x = a.ld_x;
-  g.q = reinterpret_cast<uint8_t*>(a.q);
-  g.ld_q = a.ld_q;
+static CastGeom make_geom(const void* x, b2x_dtype xt, int64_t rows, int64_t cols, int64_t ld_x, void* q,
+                          int64_t ld_q, bool flatten) {
+  CastGeom g{};
+  g.x = x;
+  g.rows = rows;
+  g.cols = cols;
+  g.ld_x = ld_x;
+  g.q = reinterpret_cast<uint8_t*>(q);
+  g.ld_q = ld_q;
   // A contiguous tensor is one long row: fewer divisions, same elements.
-  if (a.ld_x == a.cols && a.ld_q == a.cols &&
-      (a.mode == B2X_SCALE_NONE || a.mode == B2X_SCALE_TENSOR || a.mode == B2X_SCALE_TENSOR_GIVEN)) {
-    g.cols = a.rows * a.cols;
+  if (flatten && ld_x == cols && (q == nullptr || ld_q == cols)) {
+    g.cols = rows * cols;
     g.rows = 1;
   }
-  g.segs_per_row = (g.cols + 127) / 128;
+  g.segs_per_row = (g.cols + kSeg - 1) / kSeg;
   g.nsegs = g.rows * g.segs_per_row;
-  const int es = a.x_type == B2X_F32 ? 4 : 2;
-  const int vb = es * 4;  // bytes per lane load
-  g.x_vec = ((uintptr_t)a.x % vb == 0) && ((g.rows == 1) || ((g.ld_x * es) % vb == 0));
-  g.q_vec = ((uintptr_t)a.q % 4 == 0) && ((g.rows == 1) || (g.ld_q % 4 == 0));
+  const int es = xt == B2X_F32 ? 4 : 2;
+  g.x_vec = ((uintptr_t)x % 16 == 0) && ((g.rows == 1) || ((g.ld_x * es) % 16 == 0));
+  g.q_vec = ((uintptr_t)q % 8 == 0) && ((g.rows == 1) || (g.ld_q % 8 == 0));
+  return g;
+}
+
+cudaError_t launch_cast(const b2x_cast_args& a, int num_sms, cudaStream_t st) {
+  const bool uniform = a.mode == B2X_SCALE_NONE || a.mode == B2X_SCALE_TENSOR || a.mode == B2X_SCALE_TENSOR_GIVEN;
+  CastGeom g = make_geom(a.x, a.x_type, a.rows, a.cols, a.ld_x, a.q, a.ld_q, uniform);
   uint32_t* partials = reinterpret_cast<uint32_t*>(a.workspace);
   const int fp8 = a.q_type == B2X_E4M3 ? 0 : 1;
   if (a.x_type == B2X_F32)
@@ -441,24 +471,17 @@ cudaError_t launch_cast(const b2x_cast_args& a, int num_sms, cudaStream_t st) {
 
 cudaError_t launch_amax(const void* x, b2x_dtype xt, int64_t rows, int64_t cols, int64_t ld_x, float* out,
                         uint32_t* partials, int num_sms, cudaStream_t st) {
-  CastGeom g{};
-  g.x = x;
-  g.rows = rows;
-  g.cols = cols;
-  g.ld_x = ld_x;
-  if (ld_x == cols) {
-    g.cols = rows * cols;
-    g.rows = 1;
+  CastGeom g = make_geom(x, xt, rows, cols, ld_x, nullptr, 0, true);
+  int np;
+  if (xt == B2X_F32) {
+    auto k = amax_partial_kernel<float, 4>;
+    np = grid_for(g.nsegs, 4, std::min(8, resident_ctas(k)), num_sms);
+    k<<<np, 256, 0, st>>>(g, partials);
+  } else {
+    auto k = amax_partial_kernel<uint16_t, 4>;
+    np = grid_for(g.nsegs, 4, std::min(8, resident_ctas(k)), num_sms);
+    k<<<np, 256, 0, st>>>(g, partials);
   }
-  g.segs_per_row = (g.cols + 127) / 128;
-  g.nsegs = g.rows * g.segs_per_row;
-  const int es = xt == B2X_F32 ? 4 : 2;
-  g.x_vec = ((uintptr_t)x % (es * 4) == 0) && ((g.rows == 1) || ((g.ld_x * es) % (es * 4) == 0));
-  int np = cast_num_partials(g.nsegs, num_sms);
-  if (xt == B2X_F32)
-    amax_partial_kernel<float, 4><<<np, 256, 0, st>>>(g, partials);
-  else
-    amax_partial_kernel<uint16_t, 4><<<np, 256, 0, st>>>(g, partials);
   amax_final_kernel<<<1, 256, 0, st>>>(partials, np, out);
   note_launch(2);
   return cudaGetLastError();
