@@ -211,6 +211,18 @@ B2X_API b2x_status b2x_fp8_gemm_splitk_noalloc(const b2x_gemm_args* args, void* 
 B2X_API const char* b2x_last_error(void);
 /* Reads and clears the device status word of the current device (blocking). */
 B2X_API b2x_status b2x_read_device_status(int* status_out);
+/*
+ * Wait-cycle trace of the last GEMM launches (diagnostics).  When the
+ * environment variable B2X_TRACE=1 is set at the first GEMM call, every GEMM
+ * kernel adds, per CTA, the clock cycles each role spent waiting into 8
+ * counters: [0] producer waiting for a free stage, [1] MMA waiting for
+ * loaded data, [2] MMA waiting for a free accumulator, [3]/[4] epilogue
+ * warpgroup 0/1 waiting for an accumulator, [5] CTA lifetime, [6] MMA issue (from data ready to commit),
+ * [7] tiles or K blocks processed.  Copies max_ctas x 8 counters to `out`
+ * (blocking) and clears them.  Counterpart of the reference's clock64-based
+ * timing (tlx.clock64, extensions/utlx/tlx/language/tlx/utility.py:108).
+ */
+B2X_API b2x_status b2x_trace_read(uint64_t* out, int max_ctas, int* n_ctas);
 /* ABI version of the loaded library (B2X_ABI_VERSION). */
 B2X_API int b2x_abi_version(void);
 /* Number of kernels this library launched since load (all devices). */

@@ -133,6 +133,21 @@ def b2x_status_ok():
     return _b2x().read_device_status() == 0
 
 
+@pytest.mark.parametrize("M", [1, 7, 16, 17, 33, 64])
+@pytest.mark.parametrize("split_k", [1, 3])
+@pytest.mark.parametrize("b_layout", ["kmajor", "rowmajor"])
+def test_small_m_paths(M, split_k, b_layout):
+    """M <= 64: the operand-swapped kernel (K-major B) and the 64-row-A kernel (row-major B)."""
+    N, K = 520, 2048
+    a, sa = _quant((M, K), O.E4M3, 31 + M)
+    b, sb = _quant((K, N), O.E4M3, 32)
+    ref = O.gemm(a, b, scale_mode="tensor", scale_a=sa, scale_b=sb)
+    ad, bd = O.fp8_bits_to_f64(a, O.E4M3) * sa, O.fp8_bits_to_f64(b, O.E4M3) * sb
+    for rep in range(2):
+        c = _gemm(a, b, O.E4M3, O.E4M3, sa, sb, b_layout, config={"SPLIT_K": split_k})
+        _check(c, ref, ad, bd, f"M={M} split={split_k} {b_layout} rep={rep}")
+
+
 def test_splitk_decode_shape_full():
     """BASELINE config: M=64 N=8192 K=28672, SPLIT_K=8, per-tensor e4m3, bf16 out.
     Checked against the oracle on a sample of 512 output columns."""

@@ -26,6 +26,7 @@ EXPORTED = (
     "b2x_cast_workspace_size", "b2x_fp8_cast", "b2x_amax", "b2x_gemm_default_config",
     "b2x_gemm_workspace_size", "b2x_fp8_gemm", "b2x_splitk_reduce", "b2x_last_error",
     "b2x_read_device_status", "b2x_abi_version", "b2x_launch_count", "b2x_fp8_gemm_splitk_noalloc",
+    "b2x_trace_read",
 )
 
 
@@ -103,6 +104,8 @@ def lib() -> ctypes.CDLL:
         L.b2x_gemm_workspace_size.restype = ctypes.c_size_t
         L.b2x_fp8_gemm.argtypes = [ctypes.POINTER(GemmArgs), ctypes.c_void_p]
         L.b2x_fp8_gemm.restype = ctypes.c_int
+        L.b2x_trace_read.argtypes = [ctypes.c_void_p, ctypes.c_int, ctypes.POINTER(ctypes.c_int)]
+        L.b2x_trace_read.restype = ctypes.c_int
         L.b2x_fp8_gemm_splitk_noalloc.argtypes = [ctypes.POINTER(GemmArgs), ctypes.c_void_p]
         L.b2x_fp8_gemm_splitk_noalloc.restype = ctypes.c_int
         L.b2x_splitk_reduce.argtypes = [ctypes.c_void_p, ctypes.c_int, ctypes.c_void_p, ctypes.c_int,
@@ -129,6 +132,15 @@ def check(status: int) -> None:
 
 def launch_count() -> int:
     return int(lib().b2x_launch_count())
+
+
+def read_trace(max_ctas: int = 148):
+    """Per-CTA wait-cycle counters of the GEMM kernels (see b2x_trace_read)."""
+    import numpy as np
+    buf = np.zeros((max_ctas, 8), np.uint64)
+    n = ctypes.c_int(0)
+    check(lib().b2x_trace_read(buf.ctypes.data, max_ctas, ctypes.byref(n)))
+    return buf[: n.value]
 
 
 def read_device_status() -> int:

@@ -40,6 +40,7 @@ from . import ops
 
 _printed_heuristic_configs = set()
 _autotune_cache: dict = {}
+_config_cache: dict = {}
 
 
 @functools.lru_cache(maxsize=None)
@@ -320,13 +321,13 @@ def _autotune(a, b, scale_a, scale_b, mode, out_dtype):
     best, best_t = cands[0], float("inf")
     for c in cands:
         try:
-            ops.fp8_gemm_op(a, b, scale_a, scale_b, mode, out_dtype, c)
+            ops.fp8_gemm_fast(a, b, scale_a, scale_b, mode, out_dtype, tuple(c))
         except Exception:
             continue
         st, en = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         st.record()
         for _ in range(3):
-            ops.fp8_gemm_op(a, b, scale_a, scale_b, mode, out_dtype, c)
+            ops.fp8_gemm_fast(a, b, scale_a, scale_b, mode, out_dtype, tuple(c))
         en.record()
         en.synchronize()
         t = st.elapsed_time(en)
@@ -354,9 +355,11 @@ def matmul(a, b, config=None, use_heuristic=False, *, scale_a: Optional[torch.Te
     N = b.shape[1]
     out_dtype = out_dtype or torch.bfloat16
     mode = _scale_mode(scale_a, scale_b)
-    if scale_a is not None and mode == "tensor":
-        scale_a = scale_a.reshape(1).to(torch.float32)
-        scale_b = scale_b.reshape(1).to(torch.float32)
+    if mode == "tensor":
+        if scale_a.dtype != torch.float32:
+            scale_a = scale_a.to(torch.float32)
+        if scale_b.dtype != torch.float32:
+            scale_b = scale_b.to(torch.float32)
     if config is None and use_heuristic:
         config = get_heuristic_config(M, N, K, _get_num_sms(a.device.index or 0))
         if config is not None and os.environ.get("TRITON_PRINT_AUTOTUNING") == "1" and (M, N, K) not in _printed_heuristic_configs:
@@ -364,15 +367,25 @@ def matmul(a, b, config=None, use_heuristic=False, *, scale_a: Optional[torch.Te
             s = ", ".join(f"{k}: {v}" for k, v in config.items() if k not in ("pre_hook", "ctas_per_cga"))
             print(f"heuristic config selected: {s};")
     if config is not None:
-        cfg = dict(config)
-        cfg.pop("ctas_per_cga", None)
-        cfg.pop("pre_hook", None)
-        if mode == "block":
-            cfg["BLOCK_SIZE_N"], cfg["SPLIT_K"] = 128, 1
-        fields = _to_b2x_config(cfg, K)
+        try:
+            ckey = (K, mode, tuple(sorted(config.items())))
+            fields = _config_cache.get(ckey)
+        except TypeError:  # unhashable values in the dict
+            ckey, fields = None, None
+        if fields is None:
+            cfg = dict(config)
+            cfg.pop("ctas_per_cga", None)
+            cfg.pop("pre_hook", None)
+            if mode == "block":
+                cfg["BLOCK_SIZE_N"], cfg["SPLIT_K"] = 128, 1
+            fields = tuple(_to_b2x_config(cfg, K))
+            if ckey is not None:
+                _config_cache[ckey] = fields
     else:
-        fields = _autotune(a, b, scale_a, scale_b, mode, out_dtype)
-    return ops.fp8_gemm_op(a, b, scale_a, scale_b, mode, out_dtype, fields)
+        fields = tuple(_autotune(a, b, scale_a, scale_b, mode, out_dtype))
+    if torch.compiler.is_compiling():
+        return ops.fp8_gemm_op(a, b, scale_a, scale_b, mode, out_dtype, list(fields))
+    return ops.fp8_gemm_fast(a, b, scale_a, scale_b, mode, out_dtype, fields)
 
 
 def reduce_k(workspace, c, M, N, SPLIT_K):

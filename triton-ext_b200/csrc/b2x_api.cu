@@ -80,6 +80,22 @@ static PFN_cuTensorMapEncodeTiled_v12000 get_encode_fn() {
   return fn;
 }
 
+// 3-D map over a row-major [rows, K] byte matrix viewed as {128-byte K
+// chunk x, row, chunk index}: a box {128, box_rows, chunks} lands in smem as
+// `chunks` consecutive [box_rows x 128 B] 128B-swizzled tiles.
+static bool encode_chunked_3d(CUtensorMap* m, const void* base, uint64_t K, uint64_t rows, uint64_t ld_bytes,
+                              uint32_t box_rows, uint32_t chunks) {
+  auto fn = get_encode_fn();
+  if (!fn || K % 128 != 0) return false;
+  cuuint64_t dims[3] = {128, rows, K / 128};
+  cuuint64_t strides[2] = {ld_bytes, 128};
+  cuuint32_t box[3] = {128, box_rows, chunks};
+  cuuint32_t es[3] = {1, 1, 1};
+  return fn(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, const_cast<void*>(base), dims, strides, box, es,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
 // 2-D tensor map: dims {inner, outer}, row stride in bytes, box {bi, bo}.
 static b2x_status encode_2d(CUtensorMap* m, CUtensorMapDataType dt, const void* base, uint64_t inner, uint64_t outer,
                             uint64_t row_stride_bytes, uint32_t bi, uint32_t bo, CUtensorMapSwizzle sw,
@@ -227,20 +243,49 @@ b2x_status b2x_gemm_default_config(const b2x_gemm_args* a, b2x_gemm_config* out)
     c.block_n = 128;  // B scales are per 128x128 tile: one scale per N tile and K block
     c.split_k = 1;
   }
+  // M <= 64 with a K-major B runs the operand-swapped small-M kernel: 128
+  // weight rows per unit (fp8_gemm_smallm.cu).
+  const bool swap_ab = a->M <= 64 && !b_mn && !blockscaled && (c.block_n == 0 || c.block_n == 128);
+  if (swap_ab) c.block_n = 128;
   if (c.block_n == 0) {
-    // Prefer 256-wide tiles (lower shared-memory read traffic per MMA); take
-    // 128 when it clearly fills the last wave better.
+    // Score each tile shape by how well its units fill the last wave, times
+    // its per-SM throughput relative to paired 256x256 tiles (pairs read a
+    // third less operand data per SM than one CTA's 128x256 tile, which in
+    // turn reads less per FLOP than 128x128).
+    struct Cand { int bn, ctas; double weight; };
+    const Cand cands[3] = {{256, 2, 1.0}, {256, 1, 0.90}, {128, 1, 0.82}};
     double best = -1;
-    int cands[2] = {256, 128};
-    for (int bn : cands) {
-      int64_t units = (int64_t)ceil_div(a->M, 128) * ceil_div(a->N, bn);
-      int64_t waves = (units + sms - 1) / sms;
-      double eff = (double)units / (double)(waves * sms) * (bn == 256 ? 1.0 : 0.93);
-      if (eff > best + 1e-9) best = eff, c.block_n = bn;
+    for (const Cand& cd : cands) {
+      if (cd.ctas == 2 && (a->M <= 128 || blockscaled || (c.split_k > 1) || c.num_ctas == 1)) continue;
+      if (cd.ctas == 1 && c.num_ctas == 2) continue;
+      const int64_t rows = cd.ctas == 2 ? 256 : 128;
+      const int64_t slots = cd.ctas == 2 ? sms / 2 : sms;
+      int64_t units = (int64_t)ceil_div(a->M, rows) * ceil_div(a->N, cd.bn);
+      int64_t waves = (units + slots - 1) / slots;
+      double eff = (double)units / (double)(waves * slots) * cd.weight;
+      if (eff > best + 1e-9) {
+        best = eff;
+        c.block_n = cd.bn;
+        if (a->config.num_ctas == 0) c.num_ctas = cd.ctas;
+      }
     }
-    if (a->N <= 64 && !b_mn) c.block_n = 64;
+    if (a->N <= 64 && !b_mn) c.block_n = 64, c.num_ctas = a->config.num_ctas;
   }
   const int k_tiles = ceil_div(a->K, 128);
+  if (c.split_k > 1 && a->config.block_n == 0 && !blockscaled && !swap_ab) {
+    // Split-K requested without a tile width: take the width whose units
+    // fill the last wave best (decode shapes are bandwidth-bound and want
+    // every SM streaming B).
+    double best = -1;
+    int bns[3] = {256, 128, 64};
+    for (int bn : bns) {
+      if (b_mn && bn < 128) continue;
+      int64_t units = (int64_t)ceil_div(a->M, 128) * ceil_div(a->N, bn) * c.split_k;
+      int64_t waves = (units + sms - 1) / sms;
+      double eff = (double)units / (double)(waves * sms);
+      if (eff > best + 1e-3) best = eff, c.block_n = bn;
+    }
+  }
   if (c.split_k == 0) {
     // Split-K only when the output tiles cannot fill the GPU, each split
     // keeps >= 4 K blocks (the gating of preprocess_configs :487-497).
@@ -255,6 +300,7 @@ b2x_status b2x_gemm_default_config(const b2x_gemm_args* a, b2x_gemm_config* out)
       for (int bn : bns) {
         if (b_mn && bn < 128) continue;
         if (a->config.block_n && bn != a->config.block_n) continue;
+        if (swap_ab && bn != 128) continue;
         int64_t mnb = (int64_t)ceil_div(a->M, 128) * ceil_div(a->N, bn);
         for (int sk = 1; sk <= 16; ++sk) {
           if (k_tiles < sk || k_tiles / sk < 4) break;
@@ -405,6 +451,13 @@ b2x_status b2x_fp8_gemm(const b2x_gemm_args* a, void* stream) {
   g.ldc = a->ldc;
   g.num_sms = device_num_sms(dev);
   g.pair = c.num_ctas == 2 ? 1 : 0;
+  static const int trace_env = [] {
+    const char* v = getenv("B2X_TRACE");
+    return v && v[0] == '1' ? 1 : 0;
+  }();
+  g.trace = trace_env;
+  g.small_m = (!g.pair && !blockscaled && a->M <= 64) ? 1 : 0;
+  g.swap_ab = (g.small_m && !b_mn && c.block_n == 128) ? 1 : 0;
   if (c.split_k > 1) {
     g.ws = reinterpret_cast<float*>(a->workspace);
     g.counters = reinterpret_cast<int*>(reinterpret_cast<uint8_t*>(a->workspace) +
@@ -412,7 +465,8 @@ b2x_status b2x_fp8_gemm(const b2x_gemm_args* a, void* stream) {
   }
 
   s = encode_2d(&g.tmA, CU_TENSOR_MAP_DATA_TYPE_UINT8, a->a, (uint64_t)a->K, (uint64_t)a->M, (uint64_t)a->lda, 128,
-                128, CU_TENSOR_MAP_SWIZZLE_128B, "A");
+                g.swap_ab ? (uint32_t)smallm_tokens_tile(a->M) : (g.small_m ? 64u : 128u),
+                CU_TENSOR_MAP_SWIZZLE_128B, "A");
   if (s != B2X_OK) return s;
   if (b_mn)
     s = encode_2d(&g.tmB, CU_TENSOR_MAP_DATA_TYPE_UINT8, a->b, (uint64_t)a->N, (uint64_t)a->K, (uint64_t)a->ldb_k,
@@ -424,14 +478,40 @@ b2x_status b2x_fp8_gemm(const b2x_gemm_args* a, void* stream) {
   s = encode_2d(&g.tmC, a->c_type == B2X_F16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16,
                 a->c, (uint64_t)a->N, (uint64_t)a->M, (uint64_t)a->ldc * 2, 64, 128, CU_TENSOR_MAP_SWIZZLE_128B, "C");
   if (s != B2X_OK) return s;
+  if (g.small_m && !b_mn && !g.swap_ab) {
+    CUtensorMap a3, b3;
+    // K blocks per stage of the small-M kernel (MShape in fp8_gemm.cu).
+    const uint32_t kps = c.block_n == 64 ? 4 : (c.block_n == 128 ? 2 : 1);
+    if (encode_chunked_3d(&a3, a->a, (uint64_t)a->K, (uint64_t)a->M, (uint64_t)a->lda, 64, kps) &&
+        encode_chunked_3d(&b3, a->b, (uint64_t)a->K, (uint64_t)a->N, (uint64_t)a->ldb_n, (uint32_t)c.block_n, kps)) {
+      g.tmA = a3;
+      g.tmB = b3;
+      g.chunk3d = 1;
+    }
+  }
 
   if (blockscaled)
     e = launch_fp8_gemm_blockscaled(g, (cudaStream_t)stream);
   else if (g.pair)
     e = launch_fp8_gemm_pair(g, (cudaStream_t)stream);
+  else if (g.swap_ab)
+    e = launch_fp8_gemm_smallm(g, (cudaStream_t)stream);
   else
     e = launch_fp8_gemm(g, (cudaStream_t)stream);
   if (e != cudaSuccess) return cuda_fail(e, "b2x_fp8_gemm launch");
+  return B2X_OK;
+}
+
+b2x_status b2x_trace_read(uint64_t* out, int max_ctas, int* n_ctas) {
+  t_err[0] = 0;
+  if (!out || max_ctas <= 0) return fail(B2X_ERR_INVALID_ARG, "b2x_trace_read: bad output buffer");
+  const int n = max_ctas < kTraceMaxCtas ? max_ctas : kTraceMaxCtas;
+  cudaError_t e = cudaMemcpyFromSymbol(out, g_trace, sizeof(unsigned long long) * kTraceSlots * n);
+  if (e != cudaSuccess) return cuda_fail(e, "reading the trace counters");
+  static unsigned long long zeros[kTraceMaxCtas * kTraceSlots];
+  e = cudaMemcpyToSymbol(g_trace, zeros, sizeof(zeros));
+  if (e != cudaSuccess) return cuda_fail(e, "clearing the trace counters");
+  if (n_ctas) *n_ctas = n;
   return B2X_OK;
 }
 

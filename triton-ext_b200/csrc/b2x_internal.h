@@ -39,9 +39,15 @@ struct GemmLaunch {
   int64_t ldc;
   int num_sms;
   int pair;          // paired-CTA (cta_group::2) 256x256 tiles
+  int small_m;       // M <= 64: 64-row A boxes, 4 K blocks per stage
+  int chunk3d;       // small_m with 3-D (x, row, K chunk) A/B tensor maps
+  int swap_ab;       // small_m with K-major B: weights on the MMA's M side
+  int trace;         // B2X_TRACE=1: per-CTA wait cycles into g_trace
 };
 
 cudaError_t launch_fp8_gemm(const GemmLaunch& g, cudaStream_t st);
+cudaError_t launch_fp8_gemm_smallm(const GemmLaunch& g, cudaStream_t st);
+int smallm_tokens_tile(int64_t M);
 cudaError_t launch_fp8_gemm_pair(const GemmLaunch& g, cudaStream_t st);
 cudaError_t launch_fp8_gemm_blockscaled(const GemmLaunch& g, cudaStream_t st);
 cudaError_t launch_splitk_reduce(const void* ws, b2x_dtype wt, void* c, b2x_dtype ct, int64_t M, int64_t N,

@@ -4,6 +4,7 @@
 #include "fp8_cast.cu"
 #include "fp8_gemm.cu"
 #include "fp8_gemm_pair.cu"
+#include "fp8_gemm_smallm.cu"
 #include "fp8_gemm_blockscaled.cu"
 #include "splitk_reduce.cu"
 #include "fp8_gemm_noalloc.cu"

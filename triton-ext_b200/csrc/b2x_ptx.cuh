@@ -105,6 +105,31 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volati
   }
 }
 
+// ---------------------------------------------------------------- tracing
+// Optional per-CTA cycle counters (enabled per launch by B2X_TRACE=1 on the
+// host; read back with b2x_trace_read).  Slots:
+//   0 producer waiting for a free stage     1 MMA waiting for loaded data
+//   2 MMA waiting for a free accumulator    3 epilogue WG0 waiting for data
+//   4 epilogue WG1 waiting for data         5 CTA lifetime (thread 0)
+//   6 MMA issue (data ready to commit)      7 units processed by the CTA
+constexpr int kTraceSlots = 8;
+constexpr int kTraceMaxCtas = 512;
+__device__ unsigned long long g_trace[kTraceMaxCtas * kTraceSlots];
+
+__device__ __forceinline__ void trace_add(int on, int slot, unsigned long long v) {
+  if (on && blockIdx.x < kTraceMaxCtas) atomicAdd(&g_trace[blockIdx.x * kTraceSlots + slot], v);
+}
+
+// Bounded wait that also adds the cycles it spent to trace slot `slot`.
+__device__ __forceinline__ bool mbar_wait_traced(uint64_t* bar, uint32_t parity, volatile int* abort, int code,
+                                                 int trace, int slot) {
+  if (!trace) return mbar_wait(bar, parity, abort, code);
+  const long long t0 = clock64();
+  const bool ok = mbar_wait(bar, parity, abort, code);
+  trace_add(1, slot, (unsigned long long)(clock64() - t0));
+  return ok;
+}
+
 // Named barrier among `count` threads (multiple of 32).
 __device__ __forceinline__ void named_bar_sync(uint32_t id, uint32_t count) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");
@@ -123,6 +148,16 @@ __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* m, uin
       "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes.L2::cache_hint"
       " [%0], [%1, {%3, %4}], [%2], %5;" ::"r"(smem_u32(dst)),
       "l"(reinterpret_cast<uint64_t>(m)), "r"(smem_u32(bar)), "r"(x), "r"(y), "l"(policy)
+      : "memory");
+}
+
+// 3-D tiled load (x innermost), completion counted on `bar` in bytes.
+__device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* m, uint64_t* bar, int32_t x, int32_t y,
+                                            int32_t z, uint64_t policy) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes.L2::cache_hint"
+      " [%0], [%1, {%3, %4, %5}], [%2], %6;" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(m)), "r"(smem_u32(bar)), "r"(x), "r"(y), "r"(z), "l"(policy)
       : "memory");
 }
 
@@ -313,6 +348,16 @@ __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
   uint32_t r;
   asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
   return r;
+}
+
+__device__ __forceinline__ int atomic_add_acq_rel_gpu(int* p, int v) {
+  int old;
+  asm volatile("atom.acq_rel.gpu.global.add.s32 %0, [%1], %2;" : "=r"(old) : "l"(p), "r"(v) : "memory");
+  return old;
+}
+
+__device__ __forceinline__ void red_add_f32(float* p, float a) {
+  asm volatile("red.global.add.f32 [%0], %1;" ::"l"(p), "f"(a) : "memory");
 }
 
 // Vectorised split-K reduction: four fp32 adds in one global reduction.

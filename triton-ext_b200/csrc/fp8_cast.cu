@@ -18,6 +18,7 @@
 // enough bytes in flight for HBM3e.
 #include <cuda_bf16.h>
 #include <algorithm>
+#include <cstring>
 #include <cstdint>
 #include "b2x_ptx.cuh"
 #include "b2x_internal.h"
@@ -74,35 +75,66 @@ __device__ __forceinline__ float bf16hi(uint32_t u) { return __uint_as_float(u &
 constexpr int kSeg = 256;  // columns per warp step
 constexpr int kLaneElems = 8;
 
+// Eight consecutive input elements as loaded: kept packed (2 x 16 B of fp32
+// or 16 B of bf16) until they are converted, so deep unrolling costs few
+// registers and many loads can be in flight per thread.
+template <typename T>
+struct Raw8;
+template <>
+struct Raw8<float> {
+  float4 a, b;
+};
+template <>
+struct Raw8<uint16_t> {
+  uint4 a;
+};
+
 // Load 8 consecutive elements from column `col` of a row; elements at or
 // beyond `cols` read as 0.  `vec_ok`: the row base is 16-byte aligned.
-template <typename T>
-__device__ __forceinline__ void load8(const T* row, int64_t col, int64_t cols, bool vec_ok, float (&v)[8]);
-
-template <>
-__device__ __forceinline__ void load8<float>(const float* row, int64_t col, int64_t cols, bool vec_ok,
-                                             float (&v)[8]) {
+__device__ __forceinline__ void load_raw(const float* row, int64_t col, int64_t cols, bool vec_ok, Raw8<float>& r) {
   if (vec_ok && col + 7 < cols) {
-    float4 a = __ldcs(reinterpret_cast<const float4*>(row + col));
-    float4 b = __ldcs(reinterpret_cast<const float4*>(row + col + 4));
-    v[0] = a.x, v[1] = a.y, v[2] = a.z, v[3] = a.w, v[4] = b.x, v[5] = b.y, v[6] = b.z, v[7] = b.w;
+    r.a = __ldcs(reinterpret_cast<const float4*>(row + col));
+    r.b = __ldcs(reinterpret_cast<const float4*>(row + col + 4));
     return;
   }
+  float v[8];
 #pragma unroll
   for (int i = 0; i < 8; ++i) v[i] = (col + i < cols) ? row[col + i] : 0.f;
+  r.a = make_float4(v[0], v[1], v[2], v[3]);
+  r.b = make_float4(v[4], v[5], v[6], v[7]);
 }
 
-template <>
-__device__ __forceinline__ void load8<uint16_t>(const uint16_t* row, int64_t col, int64_t cols, bool vec_ok,
-                                                float (&v)[8]) {
+__device__ __forceinline__ void load_raw(const uint16_t* row, int64_t col, int64_t cols, bool vec_ok,
+                                         Raw8<uint16_t>& r) {
   if (vec_ok && col + 7 < cols) {
-    uint4 u = __ldcs(reinterpret_cast<const uint4*>(row + col));
-    v[0] = bf16lo(u.x), v[1] = bf16hi(u.x), v[2] = bf16lo(u.y), v[3] = bf16hi(u.y);
-    v[4] = bf16lo(u.z), v[5] = bf16hi(u.z), v[6] = bf16lo(u.w), v[7] = bf16hi(u.w);
+    r.a = __ldcs(reinterpret_cast<const uint4*>(row + col));
     return;
   }
+  uint32_t w[4] = {0, 0, 0, 0};
 #pragma unroll
-  for (int i = 0; i < 8; ++i) v[i] = (col + i < cols) ? bf16_bits_to_f32(row[col + i]) : 0.f;
+  for (int i = 0; i < 8; ++i)
+    if (col + i < cols) w[i >> 1] |= (uint32_t)row[col + i] << (16 * (i & 1));
+  r.a = make_uint4(w[0], w[1], w[2], w[3]);
+}
+
+template <typename T>
+__device__ __forceinline__ void zero_raw(Raw8<T>& r) {
+  memset(&r, 0, sizeof(r));
+}
+
+__device__ __forceinline__ void unpack(const Raw8<float>& r, float (&v)[8]) {
+  v[0] = r.a.x, v[1] = r.a.y, v[2] = r.a.z, v[3] = r.a.w, v[4] = r.b.x, v[5] = r.b.y, v[6] = r.b.z, v[7] = r.b.w;
+}
+__device__ __forceinline__ void unpack(const Raw8<uint16_t>& r, float (&v)[8]) {
+  v[0] = bf16lo(r.a.x), v[1] = bf16hi(r.a.x), v[2] = bf16lo(r.a.y), v[3] = bf16hi(r.a.y);
+  v[4] = bf16lo(r.a.z), v[5] = bf16hi(r.a.z), v[6] = bf16lo(r.a.w), v[7] = bf16hi(r.a.w);
+}
+
+template <typename T>
+__device__ __forceinline__ void load8(const T* row, int64_t col, int64_t cols, bool vec_ok, float (&v)[8]) {
+  Raw8<T> r;
+  load_raw(row, col, cols, vec_ok, r);
+  unpack(r, v);
 }
 
 __device__ __forceinline__ void store8(uint8_t* row, int64_t col, int64_t cols, bool vec_ok, uint2 q) {
@@ -157,19 +189,22 @@ __global__ void __launch_bounds__(256) amax_partial_kernel(CastGeom g, uint32_t*
   const T* x = reinterpret_cast<const T*>(g.x);
   float m = 0.f;
   for (int64_t s0 = warp * U; s0 < g.nsegs; s0 += nwarps * U) {
-    float v[U][8];
+    Raw8<T> raw[U];
 #pragma unroll
     for (int u = 0; u < U; ++u) {
       int64_t r, c;
       seg_pos(g, s0 + u, lane, r, c);
       if (s0 + u < g.nsegs)
-        load8<T>(x + r * g.ld_x, c, g.cols, g.x_vec, v[u]);
+        load_raw(x + r * g.ld_x, c, g.cols, g.x_vec, raw[u]);
       else
-#pragma unroll
-        for (int i = 0; i < 8; ++i) v[u][i] = 0.f;
+        zero_raw(raw[u]);
     }
 #pragma unroll
-    for (int u = 0; u < U; ++u) m = fmaxf(m, absmax8(v[u]));
+    for (int u = 0; u < U; ++u) {
+      float v[8];
+      unpack(raw[u], v);
+      m = fmaxf(m, absmax8(v));
+    }
   }
 #pragma unroll
   for (int o = 16; o; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
@@ -241,17 +276,19 @@ __global__ void __launch_bounds__(256) quant_uniform_kernel(CastGeom g, int mode
   const int64_t nwarps = (int64_t)gridDim.x * (blockDim.x >> 5);
   const T* x = reinterpret_cast<const T*>(g.x);
   for (int64_t s0 = warp * U; s0 < g.nsegs; s0 += nwarps * U) {
-    float v[U][8];
+    Raw8<T> raw[U];
     int64_t rr[U], cc[U];
 #pragma unroll
     for (int u = 0; u < U; ++u) {
       seg_pos(g, s0 + u, lane, rr[u], cc[u]);
-      if (s0 + u < g.nsegs) load8<T>(x + rr[u] * g.ld_x, cc[u], g.cols, g.x_vec, v[u]);
+      if (s0 + u < g.nsegs) load_raw(x + rr[u] * g.ld_x, cc[u], g.cols, g.x_vec, raw[u]);
     }
 #pragma unroll
     for (int u = 0; u < U; ++u) {
       if (s0 + u >= g.nsegs) continue;
-      uint2 q = scaled ? quant8<FP8>(v[u], inv) : quant8<FP8, false>(v[u], inv);
+      float v[8];
+      unpack(raw[u], v);
+      uint2 q = scaled ? quant8<FP8>(v, inv) : quant8<FP8, false>(v, inv);
       store8(g.q + rr[u] * g.ld_q, cc[u], g.cols, g.q_vec, q);
     }
   }
@@ -269,23 +306,24 @@ __global__ void __launch_bounds__(256) quant_rowblock_kernel(CastGeom g, void* s
   const int64_t nwarps = (int64_t)gridDim.x * (blockDim.x >> 5);
   const T* x = reinterpret_cast<const T*>(g.x);
   for (int64_t s0 = warp * U; s0 < g.nsegs; s0 += nwarps * U) {
-    float v[U][8];
+    Raw8<T> raw[U];
     int64_t rr[U], cc[U];
 #pragma unroll
     for (int u = 0; u < U; ++u) {
       seg_pos(g, s0 + u, lane, rr[u], cc[u]);
       if (s0 + u < g.nsegs)
-        load8<T>(x + rr[u] * g.ld_x, cc[u], g.cols, g.x_vec, v[u]);
+        load_raw(x + rr[u] * g.ld_x, cc[u], g.cols, g.x_vec, raw[u]);
       else
-#pragma unroll
-        for (int i = 0; i < 8; ++i) v[u][i] = 0.f;
+        zero_raw(raw[u]);
     }
 #pragma unroll
     for (int u = 0; u < U; ++u) {
       // Lanes past the end of the row (or of the tensor) take part in the
       // shuffles holding zeros but store nothing.
       const bool live = s0 + u < g.nsegs;
-      float m = absmax8(v[u]);
+      float v[8];
+      unpack(raw[u], v);
+      float m = absmax8(v);
 #pragma unroll
       for (int o = LPG / 2; o; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
       float inv;
@@ -301,7 +339,7 @@ __global__ void __launch_bounds__(256) quant_rowblock_kernel(CastGeom g, void* s
         inv = sc == 0.f ? 0.f : __fdiv_rn(1.0f, sc);
         if (leader) reinterpret_cast<float*>(scale)[rr[u] * ld_scale + cc[u] / GROUP] = sc;
       }
-      if (live) store8(g.q + rr[u] * g.ld_q, cc[u], g.cols, g.q_vec, quant8<FP8>(v[u], inv));
+      if (live) store8(g.q + rr[u] * g.ld_q, cc[u], g.cols, g.q_vec, quant8<FP8>(v, inv));
     }
   }
 }
@@ -390,7 +428,7 @@ int cast_num_partials(int64_t nsegs, int num_sms) {
 template <typename T, int FP8>
 static cudaError_t launch_cast_t(const CastGeom& g, int mode, void* scale, int64_t ld_scale, uint32_t* partials,
                                  int num_sms, cudaStream_t st) {
-  constexpr int U = sizeof(T) == 4 ? 2 : 4;  // 64 B in flight per lane either way
+  constexpr int U = sizeof(T) == 4 ? 4 : 8;  // 128 B of loads in flight per lane either way
   switch (mode) {
     case B2X_SCALE_NONE:
     case B2X_SCALE_TENSOR_GIVEN:

@@ -30,16 +30,31 @@
 
 namespace b2x {
 
-template <int BN, int STAGES>
+// SMALLM: the variant for M <= 64 (decode shapes, HBM-bound).  A is loaded
+// as 64-row boxes (the MMA still runs M=128; rows 64-127 of its A operand are
+// whatever the neighbouring smem holds and only feed accumulator rows that
+// are never stored), and each stage holds kKPS consecutive 128-deep K blocks
+// (4 / 2 / 1 for BN = 64 / 128 / 256, about 64 KB per stage), fetched as one
+// 3-D box per operand so every row of B is read in 256-512 contiguous bytes.
+template <int SMALLM, int BN>
+struct MShape {
+  static constexpr int kARows = SMALLM ? 64 : 128;
+  static constexpr int kKPS = SMALLM ? (BN == 64 ? 4 : (BN == 128 ? 2 : 1)) : 1;
+};
+
+// SPLITK kernels reduce with red.global and need no C staging tiles.
+template <int BN, int STAGES, int SMALLM = 0, int SPLITK = 0>
 struct SmemLayout {
-  static constexpr int kABytes = kBM * kBK;        // 16 KB
-  static constexpr int kBBytes = BN * kBK;         // BN x 128 B
+  static constexpr int kASub = MShape<SMALLM, BN>::kARows * kBK;  // one K block of A
+  static constexpr int kBSub = BN * kBK;                          // one K block of B
+  static constexpr int kABytes = kASub * MShape<SMALLM, BN>::kKPS;
+  static constexpr int kBBytes = kBSub * MShape<SMALLM, BN>::kKPS;
   static constexpr int kStageBytes = kABytes + kBBytes;
   static constexpr int kCBytes = kBM * 128;        // one 128 x 128 B staging tile per epilogue warpgroup
   static constexpr int kAOff = 0;
   static constexpr int kBOff = STAGES * kABytes;
   static constexpr int kCOff = kBOff + STAGES * kBBytes;
-  static constexpr int kBarOff = kCOff + 2 * kCBytes;
+  static constexpr int kBarOff = kCOff + (SPLITK ? 0 : 2 * kCBytes);
   // barriers: full[STAGES], empty[STAGES], tfull[2], tempty[2], mma_done, + tmem slot + flags
   static constexpr int kBarBytes = (2 * STAGES + 5) * 8 + 16;
   static constexpr int kTotal = kBarOff + kBarBytes;
@@ -52,11 +67,12 @@ struct TmemCols {
   static constexpr uint32_t kAlloc = 2 * BN < 32 ? 32 : 2 * BN;
 };
 
-template <int BN, int STAGES, int B_MN, int SPLITK>
+template <int BN, int STAGES, int B_MN, int SPLITK, int SMALLM>
 __global__ void __launch_bounds__(kThreads, 1)
     fp8_gemm_ws_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                        const __grid_constant__ CUtensorMap tmC, const GemmParams p) {
-  using L = SmemLayout<BN, STAGES>;
+  using L = SmemLayout<BN, STAGES, SMALLM, SPLITK>;
+  constexpr int KPS = MShape<SMALLM, BN>::kKPS;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + L::kBarOff);
@@ -69,6 +85,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
+  const long long t_start = clock64();
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
@@ -115,22 +132,42 @@ __global__ void __launch_bounds__(kThreads, 1)
         compute_pid(mn, num_pid_in_group, p.num_pid_m, p.group_size_m, pid_m, pid_n);
         const int k0 = split * p.k_tiles_per_split;
         const int k1 = min(k0 + p.k_tiles_per_split, p.k_tiles);
-        for (int kb = k0; kb < k1; ++kb) {
-          if (!mbar_wait(&empty[stage], phase ^ 1, abort_flag, kStatusTimeoutProducer)) {
+        for (int kb = k0; kb < k1; kb += KPS) {
+          if (!mbar_wait_traced(&empty[stage], phase ^ 1, abort_flag, kStatusTimeoutProducer, p.trace, 0)) {
             ok = false;
             break;
           }
+          const int cnt = min(KPS, k1 - kb);
           uint8_t* sA = smem + L::kAOff + stage * L::kABytes;
           uint8_t* sB = smem + L::kBOff + stage * L::kBBytes;
-          mbar_arrive_expect_tx(&full[stage], L::kStageBytes);
-          tma_load_2d(sA, &tmA, &full[stage], kb * kBK, pid_m * kBM, pol_a);
-          if (B_MN) {
-            // B row-major [K, N]: slabs of 128 N-columns x 128 K-rows.
+          if (SMALLM && p.chunk3d) {
+            // One 3-D box per operand: KPS consecutive 128-byte K chunks of
+            // every row (a box always moves all KPS chunks; chunks past the
+            // end of K read as zeros and past this split are simply unused).
+            mbar_arrive_expect_tx(&full[stage], L::kStageBytes);
+            tma_load_3d(sA, &tmA, &full[stage], 0, pid_m * kBM, kb, pol_a);
+            tma_load_3d(sB, &tmB, &full[stage], 0, pid_n * BN, kb, pol_b);
+            issued_mask |= 1u << stage;
+            pend_phase[stage] = phase;
+            if (++stage == STAGES) {
+              stage = 0;
+              phase ^= 1;
+            }
+            continue;
+          }
+          mbar_arrive_expect_tx(&full[stage], cnt * (L::kASub + L::kBSub));
+          for (int j = 0; j < cnt; ++j) {
+            const int kx = (kb + j) * kBK;
+            tma_load_2d(sA + j * L::kASub, &tmA, &full[stage], kx, pid_m * kBM, pol_a);
+            if (B_MN) {
+              // B row-major [K, N]: slabs of 128 N-columns x 128 K-rows.
 #pragma unroll
-            for (int j = 0; j < (BN + 127) / 128; ++j)
-              tma_load_2d(sB + j * 128 * kBK, &tmB, &full[stage], pid_n * BN + j * 128, kb * kBK, pol_b);
-          } else {
-            tma_load_2d(sB, &tmB, &full[stage], kb * kBK, pid_n * BN, pol_b);
+              for (int s2 = 0; s2 < (BN + 127) / 128; ++s2)
+                tma_load_2d(sB + j * L::kBSub + s2 * 128 * kBK, &tmB, &full[stage], pid_n * BN + s2 * 128, kx,
+                            pol_b);
+            } else {
+              tma_load_2d(sB + j * L::kBSub, &tmB, &full[stage], kx, pid_n * BN, pol_b);
+            }
           }
           issued_mask |= 1u << stage;
           pend_phase[stage] = phase;
@@ -160,28 +197,34 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int k1 = min(k0 + p.k_tiles_per_split, p.k_tiles);
         const int buf = local & 1;
         const uint32_t use = (uint32_t)(local >> 1);
-        if (!mbar_wait(&tempty[buf], (use & 1) ^ 1, abort_flag, kStatusTimeoutMma)) {
+        trace_add(p.trace, 7, 1);
+        if (!mbar_wait_traced(&tempty[buf], (use & 1) ^ 1, abort_flag, kStatusTimeoutMma, p.trace, 2)) {
           ok = false;
           break;
         }
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + buf * TmemCols<BN>::kPerBuf;
-        for (int kb = k0; kb < k1; ++kb) {
-          if (!mbar_wait(&full[stage], phase, abort_flag, kStatusTimeoutMma)) {
+        for (int kb = k0; kb < k1; kb += KPS) {
+          if (!mbar_wait_traced(&full[stage], phase, abort_flag, kStatusTimeoutMma, p.trace, 1)) {
             ok = false;
             break;
           }
           tc_fence_after();
-          const uint32_t a_addr = smem_u32(smem + L::kAOff + stage * L::kABytes);
-          const uint32_t b_addr = smem_u32(smem + L::kBOff + stage * L::kBBytes);
+          const long long t_issue = p.trace ? clock64() : 0;
+          const int cnt = min(KPS, k1 - kb);
+          for (int j = 0; j < cnt; ++j) {
+            const uint32_t a_addr = smem_u32(smem + L::kAOff + stage * L::kABytes + j * L::kASub);
+            const uint32_t b_addr = smem_u32(smem + L::kBOff + stage * L::kBBytes + j * L::kBSub);
 #pragma unroll
-          for (int k = 0; k < kBK / 32; ++k) {
-            const uint64_t adesc = smem_desc_sw128(a_addr + k * 32, 16, 1024);
-            const uint64_t bdesc = B_MN ? smem_desc_sw128(b_addr + k * 32 * 128, 128 * kBK, 1024)
-                                        : smem_desc_sw128(b_addr + k * 32, 16, 1024);
-            mma_f8f6f4(d_tmem, adesc, bdesc, p.idesc, (kb > k0 || k > 0) ? 1u : 0u);
+            for (int k = 0; k < kBK / 32; ++k) {
+              const uint64_t adesc = smem_desc_sw128(a_addr + k * 32, 16, 1024);
+              const uint64_t bdesc = B_MN ? smem_desc_sw128(b_addr + k * 32 * 128, 128 * kBK, 1024)
+                                          : smem_desc_sw128(b_addr + k * 32, 16, 1024);
+              mma_f8f6f4(d_tmem, adesc, bdesc, p.idesc, (kb > k0 || j > 0 || k > 0) ? 1u : 0u);
+            }
           }
           mma_commit(&empty[stage]);
+          if (p.trace) trace_add(1, 6, (unsigned long long)(clock64() - t_issue));
           if (++stage == STAGES) {
             stage = 0;
             phase ^= 1;
@@ -212,7 +255,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       int pid_m, pid_n;
       compute_pid(mn, num_pid_in_group, p.num_pid_m, p.group_size_m, pid_m, pid_n);
       const uint32_t use = (uint32_t)(local >> 1);
-      bool ok = mbar_wait(&tfull[e], use & 1, abort_flag, kStatusTimeoutEpilogue);
+      bool ok = mbar_wait_traced(&tfull[e], use & 1, abort_flag, kStatusTimeoutEpilogue,
+                                 p.trace && wg_tid == 0, 3 + e);
       if (!wg_all(ok, bar_id)) break;
       tc_fence_after();
       const uint32_t t_row = tmem_base + e * TmemCols<BN>::kPerBuf + ((uint32_t)(q * 32) << 16);
@@ -241,12 +285,10 @@ __global__ void __launch_bounds__(kThreads, 1)
           // The staging tile may still be read by the previous TMA store.
           if (wg_tid == 0) bulk_wait_group_read0();
           named_bar_sync(bar_id, 128);
-          uint8_t* srow = stage_c + row * 128;
+          const uint32_t srow = smem_u32(stage_c + row * 128);
 #pragma unroll
-          for (int j = 0; j < 8; ++j) {
-            uint4 val = make_uint4(pk[4 * j], pk[4 * j + 1], pk[4 * j + 2], pk[4 * j + 3]);
-            *reinterpret_cast<uint4*>(srow + ((j ^ (row & 7)) << 4)) = val;
-          }
+          for (int j = 0; j < 8; ++j)
+            st_shared_v4(srow + ((j ^ (row & 7)) << 4), pk[4 * j], pk[4 * j + 1], pk[4 * j + 2], pk[4 * j + 3]);
           fence_proxy_async_smem();
           named_bar_sync(bar_id, 128);
           if (wg_tid == 0) {
@@ -257,13 +299,19 @@ __global__ void __launch_bounds__(kThreads, 1)
         tc_fence_before();
         mbar_arrive(&tempty[e]);
       } else {
-        // Split-K: reduce this unit's fp32 partial into the workspace.
+        // Split-K: reduce this unit's fp32 partial into the workspace.  The
+        // accumulator buffer goes back to the MMA warp as soon as its last
+        // columns are in registers, before the reductions are issued.
         const bool row_ok = grow < p.M;
 #pragma unroll 1
         for (int c0 = 0; c0 < BN; c0 += 32) {
           uint32_t v[32];
           tmem_ld_32x32b_x32(t_row + c0, v);
           tmem_ld_wait();
+          if (c0 + 32 == BN) {
+            tc_fence_before();
+            mbar_arrive(&tempty[e]);
+          }
           if (row_ok) {
             float* dst = p.ws + (int64_t)grow * p.N + n0 + c0;
 #pragma unroll
@@ -279,60 +327,54 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
           }
         }
-        tc_fence_before();
-        mbar_arrive(&tempty[e]);
         // Last unit to arrive on this tile converts the sum and re-zeroes the
-        // workspace so the next call finds it clean.
-        __threadfence();
+        // workspace so the next call finds it clean.  The warpgroup barrier
+        // orders every thread's reductions before thread 0's acq_rel counter
+        // increment (release is cumulative); the finisher's reads are ordered
+        // after it by the same increment (acquire) and the second barrier.
         named_bar_sync(bar_id, 128);
         __shared__ int s_last[2];
         if (wg_tid == 0) {
-          int old = atomicAdd(p.counters + mn, 1);
+          int old = atomic_add_acq_rel_gpu(p.counters + mn, 1);
           s_last[e] = (old == p.split_k - 1);
         }
         named_bar_sync(bar_id, 128);
         if (s_last[e]) {
-          __threadfence();
-          if (row_ok) {
-            float* src = p.ws + (int64_t)grow * p.N + n0;
-            uint8_t* crow = reinterpret_cast<uint8_t*>(p.c) + ((int64_t)grow * p.ldc + n0) * 2;
-            for (int c = 0; c < BN; c += 8) {
-              if (n0 + c >= p.N) break;
-              float f[8];
-              if (n0 + c + 7 < p.N) {
-                float4 x0 = __ldcg(reinterpret_cast<const float4*>(src + c));
-                float4 x1 = __ldcg(reinterpret_cast<const float4*>(src + c + 4));
-                f[0] = x0.x; f[1] = x0.y; f[2] = x0.z; f[3] = x0.w;
-                f[4] = x1.x; f[5] = x1.y; f[6] = x1.z; f[7] = x1.w;
-                __stcg(reinterpret_cast<float4*>(src + c), make_float4(0.f, 0.f, 0.f, 0.f));
-                __stcg(reinterpret_cast<float4*>(src + c + 4), make_float4(0.f, 0.f, 0.f, 0.f));
-                uint32_t pk[4];
+          // Finish the tile with the whole warpgroup: coalesced float4 reads of
+          // the fp32 sum (all loads of a batch issued before any store),
+          // scaled conversion to C and zeroing of the workspace behind it.
+          const int rows_v = min(kBM, p.M - m0);
+          const int cols_v = min(BN, p.N - n0);
+          const int G = cols_v >> 2;  // float4 groups per row (N % 4 == 0 for split-K)
+          const int total = rows_v * G;
+          for (int base = wg_tid; base < total; base += 128 * 8) {
+            float4 f[8];
 #pragma unroll
-                for (int i = 0; i < 4; ++i) {
-                  float lo = __fmul_rn(f[2 * i], alpha), hi = __fmul_rn(f[2 * i + 1], alpha);
-                  if (p.c_half) {
-                    __half2 h = __floats2half2_rn(lo, hi);
-                    pk[i] = *reinterpret_cast<uint32_t*>(&h);
-                  } else {
-                    pk[i] = pack_bf16x2(lo, hi);
-                  }
+            for (int u = 0; u < 8; ++u) {
+              const int idx = base + u * 128;
+              if (idx < total) {
+                const int r = idx / G, cg = idx - r * G;
+                f[u] = __ldcg(reinterpret_cast<const float4*>(p.ws + (int64_t)(m0 + r) * p.N + n0 + cg * 4));
+              }
+            }
+#pragma unroll
+            for (int u = 0; u < 8; ++u) {
+              const int idx = base + u * 128;
+              if (idx < total) {
+                const int r = idx / G, cg = idx - r * G;
+                __stcg(reinterpret_cast<float4*>(p.ws + (int64_t)(m0 + r) * p.N + n0 + cg * 4),
+                       make_float4(0.f, 0.f, 0.f, 0.f));
+                const float a0 = __fmul_rn(f[u].x, alpha), a1 = __fmul_rn(f[u].y, alpha);
+                const float a2 = __fmul_rn(f[u].z, alpha), a3 = __fmul_rn(f[u].w, alpha);
+                uint2 o;
+                if (p.c_half) {
+                  __half2 h0 = __floats2half2_rn(a0, a1), h1 = __floats2half2_rn(a2, a3);
+                  o = make_uint2(*reinterpret_cast<uint32_t*>(&h0), *reinterpret_cast<uint32_t*>(&h1));
+                } else {
+                  o = make_uint2(pack_bf16x2(a0, a1), pack_bf16x2(a2, a3));
                 }
-                if (((p.ldc & 7) == 0) && ((reinterpret_cast<uintptr_t>(p.c) & 15) == 0))
-                  *reinterpret_cast<uint4*>(crow + c * 2) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
-                else
-                  for (int i = 0; i < 4; ++i) {
-                    reinterpret_cast<uint16_t*>(crow)[c + 2 * i] = (uint16_t)(pk[i] & 0xFFFF);
-                    reinterpret_cast<uint16_t*>(crow)[c + 2 * i + 1] = (uint16_t)(pk[i] >> 16);
-                  }
-              } else {
-                for (int t = 0; t < 8 && n0 + c + t < p.N; ++t) {
-                  float s = __ldcg(src + c + t);
-                  src[c + t] = 0.f;
-                  float o = __fmul_rn(s, alpha);
-                  uint16_t h = p.c_half ? __half_as_ushort(__float2half_rn(o))
-                                        : __bfloat16_as_ushort(__float2bfloat16_rn(o));
-                  reinterpret_cast<uint16_t*>(crow)[c + t] = h;
-                }
+                *reinterpret_cast<uint2*>(reinterpret_cast<uint16_t*>(p.c) + (int64_t)(m0 + r) * p.ldc + n0 +
+                                          cg * 4) = o;
               }
             }
           }
@@ -345,6 +387,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   tc_fence_before();
   __syncthreads();
+  if (threadIdx.x == 0) trace_add(p.trace, 5, (unsigned long long)(clock64() - t_start));
   if (warp == 2) {
     tc_fence_after();
     tmem_dealloc(tmem_base, TmemCols<BN>::kAlloc);
@@ -354,11 +397,15 @@ __global__ void __launch_bounds__(kThreads, 1)
 // ----------------------------------------------------------------------------
 // Host launch.
 
-template <int BN, int STAGES, int B_MN, int SPLITK>
+template <int BN, int B_MN, int SPLITK, int SMALLM>
 static cudaError_t launch_gemm_t(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tc,
                                  const GemmParams& p, int grid, cudaStream_t st) {
-  using L = SmemLayout<BN, STAGES>;
-  auto kern = fp8_gemm_ws_kernel<BN, STAGES, B_MN, SPLITK>;
+  // Deepest ring that fits next to the two epilogue staging tiles.
+  constexpr int kStage = SmemLayout<BN, 1, SMALLM>::kStageBytes;
+  constexpr int kS0 = (kMaxDynSmem - (SPLITK ? 0 : 2 * kBM * 128) - 1024 - 256) / kStage;
+  constexpr int STAGES = kS0 > 8 ? 8 : kS0;
+  using L = SmemLayout<BN, STAGES, SMALLM, SPLITK>;
+  auto kern = fp8_gemm_ws_kernel<BN, STAGES, B_MN, SPLITK, SMALLM>;
   cudaError_t e = ensure_smem_attr(reinterpret_cast<const void*>(kern), L::kAlloc);
   if (e != cudaSuccess) return e;
   kern<<<grid, kThreads, L::kAlloc, st>>>(ta, tb, tc, p);
@@ -366,30 +413,21 @@ static cudaError_t launch_gemm_t(const CUtensorMap& ta, const CUtensorMap& tb, c
   return cudaGetLastError();
 }
 
-template <int BN, int B_MN, int SPLITK>
-static cudaError_t dispatch_stages(int stages, const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tc,
-                                   const GemmParams& p, int grid, cudaStream_t st) {
-  // Largest ring that fits next to the two epilogue staging tiles.
-  constexpr int kMaxStages = (kMaxDynSmem - 2 * kBM * 128 - 1024 - 256) / (kBM * kBK + BN * kBK);
-  constexpr int kS = kMaxStages > 8 ? 8 : kMaxStages;
-  if (stages <= 0 || stages > kS) stages = kS;
-  switch (stages) {
-    case 2: return launch_gemm_t<BN, 2, B_MN, SPLITK>(ta, tb, tc, p, grid, st);
-    case 3: return launch_gemm_t<BN, (kS >= 3 ? 3 : 2), B_MN, SPLITK>(ta, tb, tc, p, grid, st);
-    case 4: return launch_gemm_t<BN, (kS >= 4 ? 4 : 2), B_MN, SPLITK>(ta, tb, tc, p, grid, st);
-    case 5: return launch_gemm_t<BN, (kS >= 5 ? 5 : 2), B_MN, SPLITK>(ta, tb, tc, p, grid, st);
-    case 6: return launch_gemm_t<BN, (kS >= 6 ? 6 : 2), B_MN, SPLITK>(ta, tb, tc, p, grid, st);
-    default: return launch_gemm_t<BN, kS, B_MN, SPLITK>(ta, tb, tc, p, grid, st);
-  }
-}
-
 template <int B_MN, int SPLITK>
-static cudaError_t dispatch_bn(int bn, int stages, const CUtensorMap& ta, const CUtensorMap& tb,
+static cudaError_t dispatch_bn(int bn, int small_m, const CUtensorMap& ta, const CUtensorMap& tb,
                                const CUtensorMap& tc, const GemmParams& p, int grid, cudaStream_t st) {
+  if (small_m) {
+    switch (bn) {
+      case 256: return launch_gemm_t<256, B_MN, SPLITK, 1>(ta, tb, tc, p, grid, st);
+      case 128: return launch_gemm_t<128, B_MN, SPLITK, 1>(ta, tb, tc, p, grid, st);
+      case 64: return launch_gemm_t<64, B_MN, SPLITK, 1>(ta, tb, tc, p, grid, st);
+      default: return cudaErrorInvalidValue;
+    }
+  }
   switch (bn) {
-    case 256: return dispatch_stages<256, B_MN, SPLITK>(stages, ta, tb, tc, p, grid, st);
-    case 128: return dispatch_stages<128, B_MN, SPLITK>(stages, ta, tb, tc, p, grid, st);
-    case 64: return dispatch_stages<64, B_MN, SPLITK>(stages, ta, tb, tc, p, grid, st);
+    case 256: return launch_gemm_t<256, B_MN, SPLITK, 0>(ta, tb, tc, p, grid, st);
+    case 128: return launch_gemm_t<128, B_MN, SPLITK, 0>(ta, tb, tc, p, grid, st);
+    case 64: return launch_gemm_t<64, B_MN, SPLITK, 0>(ta, tb, tc, p, grid, st);
     default: return cudaErrorInvalidValue;
   }
 }
@@ -416,13 +454,15 @@ cudaError_t launch_fp8_gemm(const GemmLaunch& g, cudaStream_t st) {
   p.counters = g.counters;
   p.c = g.c;
   p.ldc = g.ldc;
+  p.chunk3d = g.chunk3d;
+  p.trace = g.trace;
   int grid = p.num_units < g.num_sms ? p.num_units : g.num_sms;
   if (g.split_k > 1) {
-    return g.b_mn ? dispatch_bn<1, 1>(g.bn, g.stages, g.tmA, g.tmB, g.tmC, p, grid, st)
-                  : dispatch_bn<0, 1>(g.bn, g.stages, g.tmA, g.tmB, g.tmC, p, grid, st);
+    return g.b_mn ? dispatch_bn<1, 1>(g.bn, g.small_m, g.tmA, g.tmB, g.tmC, p, grid, st)
+                  : dispatch_bn<0, 1>(g.bn, g.small_m, g.tmA, g.tmB, g.tmC, p, grid, st);
   }
-  return g.b_mn ? dispatch_bn<1, 0>(g.bn, g.stages, g.tmA, g.tmB, g.tmC, p, grid, st)
-                : dispatch_bn<0, 0>(g.bn, g.stages, g.tmA, g.tmB, g.tmC, p, grid, st);
+  return g.b_mn ? dispatch_bn<1, 0>(g.bn, g.small_m, g.tmA, g.tmB, g.tmC, p, grid, st)
+                : dispatch_bn<0, 0>(g.bn, g.small_m, g.tmA, g.tmB, g.tmC, p, grid, st);
 }
 
 }  // namespace b2x

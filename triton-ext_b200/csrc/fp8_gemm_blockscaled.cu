@@ -36,6 +36,7 @@ struct BsParams {
   const float* scale_a;
   const float* scale_b;
   int64_t sa_m, sa_k, sb_k, sb_n;
+  int trace;
 };
 
 template <int STAGES>
@@ -69,6 +70,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
+  const long long t_start = clock64();
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
       mbar_init(&full[s], 1);
@@ -76,7 +78,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     for (int s = 0; s < kBsSlots; ++s) {
       mbar_init(&pfull[s], 1);
-      mbar_init(&pempty[s], 256);
+      mbar_init(&pempty[s], 8);  // one arrive per epilogue warp
     }
     mbar_init(mma_done, 1);
     *abort_flag = 0;
@@ -108,7 +110,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         int pid_m, pid_n;
         compute_pid(tile, num_pid_in_group, p.num_pid_m, p.group_size_m, pid_m, pid_n);
         for (int kb = 0; kb < p.k_tiles; ++kb) {
-          if (!mbar_wait(&empty[stage], phase ^ 1, abort_flag, kStatusTimeoutProducer)) {
+          if (!mbar_wait_traced(&empty[stage], phase ^ 1, abort_flag, kStatusTimeoutProducer, p.trace, 0)) {
             ok = false;
             break;
           }
@@ -140,12 +142,13 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int tile = blockIdx.x; tile < p.num_tiles && ok; tile += gridDim.x) {
         for (int kb = 0; kb < p.k_tiles; ++kb, ++g) {
           const uint32_t slot = g % kBsSlots, use = g / kBsSlots;
-          if (!mbar_wait(&pempty[slot], (use & 1) ^ 1, abort_flag, kStatusTimeoutMma) ||
-              !mbar_wait(&full[stage], phase, abort_flag, kStatusTimeoutMma)) {
+          if (!mbar_wait_traced(&pempty[slot], (use & 1) ^ 1, abort_flag, kStatusTimeoutMma, p.trace, 2) ||
+              !mbar_wait_traced(&full[stage], phase, abort_flag, kStatusTimeoutMma, p.trace, 1)) {
             ok = false;
             break;
           }
           tc_fence_after();
+          const long long t_issue = p.trace ? clock64() : 0;
           const uint32_t a_addr = smem_u32(smem + L::kAOff + stage * L::kABytes);
           const uint32_t b_addr = smem_u32(smem + L::kBOff + stage * L::kBBytes);
           const uint32_t d_tmem = tmem_base + slot * kBsBN;
@@ -155,6 +158,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                        p.idesc, k > 0 ? 1u : 0u);
           mma_commit(&empty[stage]);
           mma_commit(&pfull[slot]);
+          if (p.trace) trace_add(1, 6, (unsigned long long)(clock64() - t_issue));
           if (++stage == STAGES) {
             stage = 0;
             phase ^= 1;
@@ -173,8 +177,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int wg_tid = threadIdx.x - (kEpiWarp0 + 4 * e) * 32;
     uint8_t* stage_c = smem + L::kCOff + e * L::kCBytes;
     uint32_t g = 0;
-    bool ok = true;
-    for (int tile = blockIdx.x; tile < p.num_tiles && ok; tile += gridDim.x) {
+    for (int tile = blockIdx.x; tile < p.num_tiles; tile += gridDim.x) {
+      bool ok = true;
       int pid_m, pid_n;
       compute_pid(tile, num_pid_in_group, p.num_pid_m, p.group_size_m, pid_m, pid_n);
       const int m0 = pid_m * kBM, n0 = pid_n * kBsBN;
@@ -194,8 +198,12 @@ __global__ void __launch_bounds__(kThreads, 1)
           sb_next = __ldg(sb_col + (int64_t)(kb + 1) * p.sb_k);
         }
         const uint32_t slot = g % kBsSlots, use = g / kBsSlots;
-        bool w = mbar_wait(&pfull[slot], use & 1, abort_flag, kStatusTimeoutEpilogue);
-        if (!wg_all(w, bar_id)) {
+        // Warp-level agreement only: no warpgroup barrier on the per-K-block
+        // path.  A warp that gave up skips its work; the warpgroup agrees at
+        // the end of the tile.
+        bool w = __all_sync(0xffffffffu, mbar_wait_traced(&pfull[slot], use & 1, abort_flag, kStatusTimeoutEpilogue,
+                                                          p.trace && wg_tid == 0, 3 + e));
+        if (!w) {
           ok = false;
           break;
         }
@@ -211,9 +219,10 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
         for (int i = 0; i < 32; ++i) acc[32 + i] = fmaf(__uint_as_float(v[i]), s, acc[32 + i]);
         tc_fence_before();
-        mbar_arrive(&pempty[slot]);
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&pempty[slot]);
       }
-      if (!ok) break;
+      if (!wg_all(ok, bar_id)) break;
       uint32_t pk[32];
 #pragma unroll
       for (int i = 0; i < 32; ++i) {
@@ -226,11 +235,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       if (wg_tid == 0) bulk_wait_group_read0();
       named_bar_sync(bar_id, 128);
-      uint8_t* srow = stage_c + row * 128;
+      const uint32_t srow = smem_u32(stage_c + row * 128);
 #pragma unroll
       for (int j = 0; j < 8; ++j)
-        *reinterpret_cast<uint4*>(srow + ((j ^ (row & 7)) << 4)) =
-            make_uint4(pk[4 * j], pk[4 * j + 1], pk[4 * j + 2], pk[4 * j + 3]);
+        st_shared_v4(srow + ((j ^ (row & 7)) << 4), pk[4 * j], pk[4 * j + 1], pk[4 * j + 2], pk[4 * j + 3]);
       fence_proxy_async_smem();
       named_bar_sync(bar_id, 128);
       if (wg_tid == 0) {
@@ -243,6 +251,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   tc_fence_before();
   __syncthreads();
+  if (threadIdx.x == 0) trace_add(p.trace, 5, (unsigned long long)(clock64() - t_start));
   if (warp == 2) {
     tc_fence_after();
     tmem_dealloc(tmem_base, kBsSlots * kBsBN);
@@ -269,6 +278,7 @@ cudaError_t launch_fp8_gemm_blockscaled(const GemmLaunch& g, cudaStream_t st) {
   p.sa_k = g.sa_stride_k;
   p.sb_k = g.sb_stride_k;
   p.sb_n = g.sb_stride_n;
+  p.trace = g.trace;
   auto kern = fp8_gemm_blockscaled_kernel<S>;
   cudaError_t e = ensure_smem_attr(reinterpret_cast<const void*>(kern), BsSmem<S>::kAlloc);
   if (e != cudaSuccess) return e;

@@ -26,6 +26,8 @@ struct GemmParams {
   int* counters;    // [num_mn_tiles] arrival counters (zero between calls)
   void* c;          // raw C pointer (split-K finisher writes directly)
   int64_t ldc;
+  int chunk3d;      // small-M kernel: A and B maps are 3-D (x, row, K chunk)
+  int trace;        // record per-CTA wait cycles in g_trace
 };
 
 // Grouped tile order, the same mapping as _compute_pid (blackwell_gemm_ws.py:433-439).
