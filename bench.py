@@ -140,64 +140,39 @@ def flush_l2(buf):
 
 
 # ----------------------------------------------------------------------------
-# the headline workload: Llama-3-70B fp8 linear set, sharded over the ranks
+# device time of short kernels: CUDA-graph replay (no host launch gaps)
 
 
-class LlamaSet:
-    def __init__(self, rank, world, dev):
-        import b2x
-        self.b2x = b2x
-        self.rank, self.world, self.dev = rank, world, dev
-        g = torch.Generator(device=dev).manual_seed(1234 + rank)
-        M, K = 8192, 8192
-        nq = LLAMA["qkv"][1] // world
-        ngu = LLAMA["gate_up"][1] // world
-        kd = LLAMA["down"][2] // world
-        self.x, self.sx = rand_fp8((M, K), g, dev)                # activations, replicated
-        self.wq, self.sq = rand_fp8((nq, K), g, dev)              # [N/g, K] weight shard
-        self.wgu, self.sgu = rand_fp8((ngu, K), g, dev)
-        self.a2, self.sa2 = rand_fp8((M, kd), g, dev)             # down input, K-sharded
-        self.wd, self.sd = rand_fp8((8192, kd), g, dev)           # down weight [N, K/g]
-        self.flops_total = sum(2.0 * m * n * k for (m, n, k) in LLAMA.values())
-        self.flops_rank = 2.0 * M * (nq * K + ngu * K + 8192 * kd)
-        self.comm_stream = torch.cuda.Stream(dev) if world > 1 else None
-        self.ev = [torch.cuda.Event(enable_timing=True) for _ in range(2)]
-        self.gu_times = []
-        self.cfg = {}
-        self.out_down = None
+def graph_ms(f, n=20):
+    for _ in range(3):
+        f()
+    torch.cuda.synchronize()
+    s = torch.cuda.Stream()
+    with torch.cuda.stream(s):
+        gr = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(gr, stream=s):
+            for _ in range(n):
+                f()
+    gr.replay()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    gr.replay()
+    e1.record()
+    e1.synchronize()
+    return e0.elapsed_time(e1) / n
 
-    def step(self, record=False):
-        b2x = self.b2x
-        mm = b2x.matmul
-        if self.world > 1:
-            # row-parallel down first, its all-reduce overlapping QKV and gate+up
-            d = mm(self.a2, self.wd.t(), self.cfg, scale_a=self.sa2, scale_b=self.sd)
-            done = torch.cuda.Event()
-            done.record()
-            with torch.cuda.stream(self.comm_stream):
-                self.comm_stream.wait_event(done)
-                dist.all_reduce(d)
-            q = mm(self.x, self.wq.t(), self.cfg, scale_a=self.sx, scale_b=self.sq)
-            if record:
-                self.ev[0].record()
-            gu = mm(self.x, self.wgu.t(), self.cfg, scale_a=self.sx, scale_b=self.sgu)
-            if record:
-                self.ev[1].record()
-            torch.cuda.current_stream().wait_stream(self.comm_stream)
-        else:
-            q = mm(self.x, self.wq.t(), self.cfg, scale_a=self.sx, scale_b=self.sq)
-            if record:
-                self.ev[0].record()
-            gu = mm(self.x, self.wgu.t(), self.cfg, scale_a=self.sx, scale_b=self.sgu)
-            if record:
-                self.ev[1].record()
-            d = mm(self.a2, self.wd.t(), self.cfg, scale_a=self.sa2, scale_b=self.sd)
-        self.out_down = d
-        return q, gu, d
 
-    def gate_up_ms(self):
-        torch.cuda.synchronize()
-        return self.ev[0].elapsed_time(self.ev[1])
+def profile_traffic(name):
+    """DRAM bytes per launch recorded from an ncu capture (profiles/*.md line
+    'traffic_bytes_per_launch: N'), or None."""
+    import re
+    try:
+        with open(os.path.join(ROOT, "profiles", name)) as f:
+            m = re.search(r"traffic_bytes_per_launch:\s*([0-9.eE+]+)", f.read())
+        return float(m.group(1)) if m else None
+    except OSError:
+        return None
 
 
 def gemm_tflops(M, N, K, iters=20, mode="tensor", cfg=None, dev="cuda"):
@@ -211,9 +186,12 @@ def gemm_tflops(M, N, K, iters=20, mode="tensor", cfg=None, dev="cuda"):
         A, sa = rand_fp8((M, K), g, dev)
         W, sw = rand_fp8((N, K), g, dev)
     f = lambda: b2x.matmul(A, W.t(), cfg if cfg is not None else {}, scale_a=sa, scale_b=sw)  # noqa: E731
-    for _ in range(3):
-        f()
-    ms = timed(f, iters)
+    if 2.0 * M * N * K < 1e11:  # short kernels: device time without host launch gaps
+        ms = graph_ms(f, iters)
+    else:
+        for _ in range(3):
+            f()
+        ms = timed(f, iters)
     return 2.0 * M * N * K / (ms * 1e-3) / 1e12, ms
 
 
@@ -252,25 +230,26 @@ def cast_gbs(dev="cuda", iters=20):
 
 def cpu_baseline_sample(seconds=10.0):
     """The C oracle (the reference's fp8 GEMM restated in C, fp32 accumulate,
-    bf16 out) on a bounded sample of the gate+up GEMM: all of K, a block of
-    rows x columns sized to about `seconds` of CPU time, on every host core."""
+    bf16 out) on a bounded sample of the gate+up GEMM: all of K=8192, a block
+    of rows x 2048 columns sized to about `seconds` of CPU time, on every host
+    core."""
     import numpy as np
     import oracle_c as OC
-    K = 8192
+    K, rows = 8192, 256
     rng = np.random.default_rng(0)
-    rows, cols = 64, 512
     a = rng.integers(0, 256, (rows, K), dtype=np.uint8) & 0x77  # finite e4m3 codes
+    b = rng.integers(0, 256, (64, K), dtype=np.uint8) & 0x77
+    t0 = time.time()
+    _, fl = OC.gemm_bf16(a, b, "e4m3", "e4m3", 1.0, 1.0)
+    rate = fl / max(time.time() - t0, 1e-4)
+    cols = int(min(57344, max(64, seconds * rate / (2.0 * rows * K))))
     b = rng.integers(0, 256, (cols, K), dtype=np.uint8) & 0x77
     t0 = time.time()
-    _, fl = OC.gemm_bf16(a, b, "e4m3", "e4m3", 1.0, 1.0, cols=(0, 64))
-    dt = max(time.time() - t0, 1e-3)
-    ncols = int(min(cols, max(64, 64 * seconds / dt / 2)))
-    t0 = time.time()
-    _, fl = OC.gemm_bf16(a, b, "e4m3", "e4m3", 1.0, 1.0, cols=(0, ncols))
+    _, fl = OC.gemm_bf16(a, b, "e4m3", "e4m3", 1.0, 1.0)
     dt = time.time() - t0
     return {"value": fl / dt / 1e12, "unit": "TFLOP/s", "cores": OC.max_threads(), "kind": "port",
-            "sample": f"gate+up GEMM rows 0..{rows} x cols 0..{ncols} x K={K} (of 8192x57344x8192), "
-                      f"{dt:.1f}s, C restatement (oracle/fp8_oracle.c) on {OC.max_threads()} threads"}
+            "sample": f"gate+up GEMM block of {rows} rows x {cols} cols x K={K} (of 8192x57344x8192), {dt:.1f} s, "
+                      f"C restatement of the reference GEMM (oracle/fp8_oracle.c) on {OC.max_threads()} threads"}
 
 
 # ----------------------------------------------------------------------------
@@ -286,8 +265,8 @@ def run_reference(args, rank, world):
     import numpy as np
     K = 8192
     rng = np.random.default_rng(0)
-    a = rng.integers(0, 256, (32, K), dtype=np.uint8) & 0x77
-    b = rng.integers(0, 256, (256, K), dtype=np.uint8) & 0x77
+    a = rng.integers(0, 256, (64, K), dtype=np.uint8) & 0x77
+    b = rng.integers(0, 256, (512, K), dtype=np.uint8) & 0x77
     for _ in range(args.warmup):
         OC.gemm_bf16(a, b, "e4m3", "e4m3", 1.0, 1.0)
     t0 = time.time()
@@ -301,9 +280,9 @@ def run_reference(args, rank, world):
         "warmup": args.warmup, "ms_per_step": dt * 1e3 / args.steps, "higher_is_better": True, "scaling": "strong",
         "vs_baseline": None, "dtype": "e4m3 in, fp32 acc, bf16 out", "data": "synthetic",
         "config": {"workload": "llama3-70b fp8 linear set @ 8192 tokens (bounded sample per step)",
-                   "sample": "32 rows x 256 cols x K=8192 of the gate+up GEMM per step"},
+                   "sample": "64 rows x 512 cols x K=8192 of the gate+up GEMM per step"},
         "cpu_baseline": {"value": v, "unit": "TFLOP/s", "cores": OC.max_threads(), "kind": "port",
-                         "sample": "32x256x8192 block of the gate+up GEMM per step, C restatement of the "
+                         "sample": "64x512x8192 block of the gate+up GEMM per step, C restatement of the "
                                    "reference GEMM (oracle/fp8_oracle.c)"},
         "e2e": {"value": v, "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
@@ -351,7 +330,8 @@ def main():
         return
 
     peaks = load_peaks()
-    ls = LlamaSet(rank, world, dev)
+    from b2x.sharded import LlamaFP8LinearSet
+    ls = LlamaFP8LinearSet(rank, world, dev)
     for _ in range(max(args.warmup, 3)):
         ls.step()
     torch.cuda.synchronize()
@@ -360,17 +340,13 @@ def main():
 
     launches0 = b2x.launch_count()
     st, en = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    gu_ms = []
     with ClockSampler(local) as clocks:
         torch.cuda.synchronize()
         if world > 1:
             dist.barrier()
         st.record()
-        for i in range(args.steps):
-            ls.step(record=True)
-            # gate+up launch duration from events on the launching stream
-            if i == args.steps - 1 or True:
-                pass
+        for _ in range(args.steps):
+            ls.step()
         en.record()
         torch.cuda.synchronize()
         if world > 1:
@@ -382,16 +358,20 @@ def main():
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
     ms_max = t.item()
 
-    # dominant kernel (gate+up GEMM): separate event-timed launches
-    for _ in range(3):
-        ls.step(record=True)
-        gu_ms.append(ls.gate_up_ms())
+    # dominant kernel (the gate+up GEMM launch): CUDA events around it on its
+    # own stream, inside full steps
+    gu_ms = []
+    for _ in range(5):
+        ev = [torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)]
+        ls.step(events=ev)
+        torch.cuda.synchronize()
+        gu_ms.append(ev[0].elapsed_time(ev[1]))
     gu = statistics.median(gu_ms)
-    M, N, K = LLAMA["gate_up"]
+    M, N, K = ls.SHAPES["gate_up"]
     gu_flops = 2.0 * M * (N // world) * K
     fp8_peak = 2.0 * peaks["bf16_sustained"]
 
-    # e2e: public API with pinned host buffers (activation in, final output back)
+    # e2e: public API with pinned host buffers (activations in, final output back)
     e2e_val, h2d, d2h = None, 0, 0
     try:
         hx = torch.empty(ls.x.shape, dtype=torch.uint8, pin_memory=True)
@@ -453,11 +433,13 @@ def main():
                        "parallelism": f"qkv/gate_up N-sharded, down K-sharded + all-reduce (x{world})",
                        "l2": "inputs larger than L2 (1.2 GB of fp8 operands per step)",
                        "tflops_per_gpu": value / world},
-            "roofline": {"bound": "tensor", "kernel": "fp8_gemm_ws_kernel (gate_up)",
+            "roofline": {"bound": "tensor", "kernel": "fp8_gemm_pair_kernel (gate+up launch)",
                          "achieved": gu_flops / (gu * 1e-3) / 1e12, "peak": fp8_peak, "unit": "TFLOP/s",
                          "frac": gu_flops / (gu * 1e-3) / 1e12 / fp8_peak,
                          "peak_source": f"2 x {peaks['source']} cuBLAS bf16 sustained (dense fp8 = 2x bf16 on B200)",
-                         "traffic": None},
+                         "frac_of_nominal_4500": gu_flops / (gu * 1e-3) / 1e12 / 4500.0,
+                         "traffic": profile_traffic("fp8_gemm_pair_kernel_llama_set.md") if world == 1 else None,
+                         "algorithmic_bytes": (8192 * 8192 + (N // world) * 8192 + 8192 * (N // world) * 2)},
             "e2e": {"value": e2e_val, "unit": "TFLOP/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
             "gpu_launches": launches,
             "clocks": clocks.summary(),

@@ -130,6 +130,7 @@ typedef struct {
   int num_smem_buffers, num_tmem_buffers;
   int num_mma_groups, epilogue_subtile;
   int num_ctas, split_k, interleave_epilogue;
+  int num_sms; /* NUM_SMS: at most this many SMs for the persistent grid (0 = all); leaves SMs free for concurrent work such as NCCL */
 } b2x_gemm_config;
 
 /*

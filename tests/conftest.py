@@ -25,3 +25,7 @@ def pytest_collection_modifyitems(config, items):
     for it in items:
         if "gpu" in it.keywords:
             it.add_marker(skip)
+
+# spawned gloo ranks import b2x / oracle from these paths too
+os.environ["PYTHONPATH"] = os.pathsep.join(
+    [os.path.join(ROOT, "triton-ext_b200"), os.path.join(ROOT, "oracle"), ROOT, os.environ.get("PYTHONPATH", "")])

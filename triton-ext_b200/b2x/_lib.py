@@ -43,7 +43,7 @@ class CastArgs(ctypes.Structure):
 class GemmConfig(ctypes.Structure):
     _fields_ = [(n, ctypes.c_int) for n in (
         "block_m", "block_n", "block_k", "group_size_m", "num_smem_buffers", "num_tmem_buffers",
-        "num_mma_groups", "epilogue_subtile", "num_ctas", "split_k", "interleave_epilogue")]
+        "num_mma_groups", "epilogue_subtile", "num_ctas", "split_k", "interleave_epilogue", "num_sms")]
 
 
 class GemmArgs(ctypes.Structure):

@@ -280,7 +280,7 @@ def _to_b2x_config(cfg: dict, K: int) -> list:
                       f"using SPLIT_K={sk}", stacklevel=3)
     return [128, bn, 128, group, 0, int(cfg.get("NUM_TMEM_BUFFERS", 2)), int(cfg.get("NUM_MMA_GROUPS", 1)),
             int(cfg.get("EPILOGUE_SUBTILE", 1)), int(cfg.get("NUM_CTAS", 0)), sk,
-            int(cfg.get("INTERLEAVE_EPILOGUE", 0))]
+            int(cfg.get("INTERLEAVE_EPILOGUE", 0)), int(cfg.get("NUM_SMS", 0))]
 
 
 def _scale_mode(scale_a, scale_b) -> str:

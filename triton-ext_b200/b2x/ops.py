@@ -27,7 +27,7 @@ CAST_MODES = {
 }
 GEMM_SCALE_MODES = {"none": L.SCALE_NONE, "tensor": L.SCALE_TENSOR, "block": L.SCALE_BLOCK_1x128}
 CONFIG_FIELDS = ("block_m", "block_n", "block_k", "group_size_m", "num_smem_buffers", "num_tmem_buffers",
-                 "num_mma_groups", "epilogue_subtile", "num_ctas", "split_k", "interleave_epilogue")
+                 "num_mma_groups", "epilogue_subtile", "num_ctas", "split_k", "interleave_epilogue", "num_sms")
 
 
 def _ptr(t: Optional[torch.Tensor]) -> Optional[int]:

@@ -1,0 +1,136 @@
+"""Multi-GPU partitioning of fp8 linear layers (one process per GPU).
+
+The reference has no multi-GPU code; the BASELINE layer set (Llama-3-70B
+shapes at 8192 tokens) is partitioned the way tensor-parallel MLP/attention
+projections are:
+
+* column-parallel (QKV, gate+up): each rank holds rows [r*N/g, (r+1)*N/g) of
+  the [N, K] weight and computes its slice of the output columns -- no
+  collective (the gate+up output stays column-sharded, which is exactly the
+  K-sharding the down projection consumes);
+* row-parallel (down): each rank holds columns [r*K/g, (r+1)*K/g) of the
+  [N, K] weight and the matching K-slice of the input, computes a partial
+  [M, N] output and the partials are summed with an all-reduce over NCCL
+  (NVLink / NVSwitch).
+
+The GEMM is injectable (`mm`) so the partitioning logic can be checked on
+CPU ranks (gloo) against an unsharded product.
+"""
+from __future__ import annotations
+
+from typing import Callable, Optional
+
+import torch
+import torch.distributed as dist
+
+
+def shard_range(n: int, rank: int, world: int):
+    """[lo, hi) of the rank's contiguous share of n items (n divisible by world)."""
+    if n % world:
+        raise ValueError(f"{n} does not split evenly over {world} ranks")
+    step = n // world
+    return rank * step, (rank + 1) * step
+
+
+def shard_rows(w: torch.Tensor, rank: int, world: int) -> torch.Tensor:
+    """Column-parallel shard of a [N, K] weight: its rows for this rank."""
+    lo, hi = shard_range(w.shape[0], rank, world)
+    return w[lo:hi].contiguous()
+
+
+def shard_cols(x: torch.Tensor, rank: int, world: int) -> torch.Tensor:
+    """Row-parallel shard of a [*, K] tensor: its K-slice for this rank."""
+    lo, hi = shard_range(x.shape[-1], rank, world)
+    return x[..., lo:hi].contiguous()
+
+
+def _default_mm(a, w, sa, sw, cfg):
+    from .blackwell_gemm_ws import matmul
+    return matmul(a, w.t(), cfg, scale_a=sa, scale_b=sw)
+
+
+def column_parallel(x, sx, w_shard, sw, mm: Callable = _default_mm, cfg: Optional[dict] = None):
+    """Local output columns: x [M, K] . w_shard[N/g, K]^T -> [M, N/g]."""
+    return mm(x, w_shard, sx, sw, cfg if cfg is not None else {})
+
+
+def row_parallel(a_shard, sa, w_shard, sw, group=None, mm: Callable = _default_mm, cfg: Optional[dict] = None,
+                 async_op: bool = False):
+    """Partial a_shard [M, K/g] . w_shard [N, K/g]^T summed over the group.
+    With async_op=True returns (partial, work) and the caller waits."""
+    part = mm(a_shard, w_shard, sa, sw, cfg if cfg is not None else {})
+    if dist.is_initialized() and dist.get_world_size(group) > 1:
+        work = dist.all_reduce(part, op=dist.ReduceOp.SUM, group=group, async_op=async_op)
+        if async_op:
+            return part, work
+    return (part, None) if async_op else part
+
+
+class LlamaFP8LinearSet:
+    """The Llama-3-70B-shaped fp8 linear set of one transformer block at a
+    fixed token count, sharded over the process group: QKV and gate+up
+    column-parallel, down row-parallel + all-reduce.
+
+    step() order on N > 1 ranks: down first, its all-reduce issued on a side
+    stream, then QKV and gate+up on the compute stream while the all-reduce
+    runs (GEMMs are launched with NUM_SMS = all but `comm_sms` SMs so NCCL's
+    kernels find free SMs).
+    """
+
+    SHAPES = {"qkv": (8192, 10240, 8192), "gate_up": (8192, 57344, 8192), "down": (8192, 8192, 28672)}
+
+    def __init__(self, rank: int, world: int, device, tokens: int = 8192, seed: int = 1234, comm_sms: int = 16,
+                 mm: Callable = _default_mm, make_input: Optional[Callable] = None):
+        self.rank, self.world, self.device, self.mm = rank, world, device, mm
+        self.tokens = tokens
+        M = tokens
+        K = self.SHAPES["qkv"][2]
+        nq = self.SHAPES["qkv"][1] // world
+        ngu = self.SHAPES["gate_up"][1] // world
+        kd = self.SHAPES["down"][2] // world
+        nd = self.SHAPES["down"][1]
+        make = make_input or _rand_fp8
+        g = torch.Generator(device=device).manual_seed(seed + rank)
+        self.x, self.sx = make((M, K), g, device)
+        self.wq, self.sq = make((nq, K), g, device)
+        self.wgu, self.sgu = make((ngu, K), g, device)
+        self.a2, self.sa2 = make((M, kd), g, device)
+        self.wd, self.sd = make((nd, kd), g, device)
+        self.flops_total = sum(2.0 * (M / 8192) * m * n * k for (m, n, k) in self.SHAPES.values())
+        self.comm_stream = torch.cuda.Stream(device) if (world > 1 and torch.device(device).type == "cuda") else None
+        n_sms = torch.cuda.get_device_properties(device).multi_processor_count if self.comm_stream else 0
+        self.overlap_cfg = {"NUM_SMS": n_sms - comm_sms} if self.comm_stream else {}
+        self.cfg = {}
+
+    def step(self, events=None):
+        """One pass over the set; returns (qkv_out, gate_up_out, down_out)."""
+        if self.world > 1 and self.comm_stream is not None:
+            d = self.mm(self.a2, self.wd, self.sa2, self.sd, self.cfg)
+            ready = torch.cuda.Event()
+            ready.record()
+            with torch.cuda.stream(self.comm_stream):
+                self.comm_stream.wait_event(ready)
+                dist.all_reduce(d)
+            d.record_stream(self.comm_stream)
+            q = self.mm(self.x, self.wq, self.sx, self.sq, self.overlap_cfg)
+            if events:
+                events[0].record()
+            gu = self.mm(self.x, self.wgu, self.sx, self.sgu, self.overlap_cfg)
+            if events:
+                events[1].record()
+            torch.cuda.current_stream().wait_stream(self.comm_stream)
+            return q, gu, d
+        q = self.mm(self.x, self.wq, self.sx, self.sq, self.cfg)
+        if events:
+            events[0].record()
+        gu = self.mm(self.x, self.wgu, self.sx, self.sgu, self.cfg)
+        if events:
+            events[1].record()
+        d = row_parallel(self.a2, self.sa2, self.wd, self.sd, mm=self.mm, cfg=self.cfg)
+        return q, gu, d
+
+
+def _rand_fp8(shape, gen, device):
+    from .ops import quantize
+    x = torch.randn(shape, device=device, generator=gen)
+    return quantize(x, "tensor", torch.float8_e4m3fn)

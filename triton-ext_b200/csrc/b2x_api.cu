@@ -450,6 +450,7 @@ b2x_status b2x_fp8_gemm(const b2x_gemm_args* a, void* stream) {
   g.c = a->c;
   g.ldc = a->ldc;
   g.num_sms = device_num_sms(dev);
+  if (c.num_sms > 0 && c.num_sms < g.num_sms) g.num_sms = c.num_sms;
   g.pair = c.num_ctas == 2 ? 1 : 0;
   static const int trace_env = [] {
     const char* v = getenv("B2X_TRACE");

@@ -283,13 +283,15 @@ static cudaError_t launch_pair_t(const GemmLaunch& g, const GemmParams& p, cudaS
   // Persistent grid: as many CTA pairs as can be resident at once.
   static int max_clusters = 0;
   if (max_clusters == 0) {
-    cfg.gridDim = dim3(2 * (g.num_sms / 2), 1, 1);
+    cfg.gridDim = dim3(2 * 74, 1, 1);
     int n = 0;
-    if (cudaOccupancyMaxActiveClusters(&n, kern, &cfg) != cudaSuccess || n <= 0) n = g.num_sms / 2;
+    if (cudaOccupancyMaxActiveClusters(&n, kern, &cfg) != cudaSuccess || n <= 0) n = 74;
     (void)cudaGetLastError();
     max_clusters = n;
   }
   int clusters = p.num_units < max_clusters ? p.num_units : max_clusters;
+  if (clusters > g.num_sms / 2) clusters = g.num_sms / 2;  // NUM_SMS cap
+  if (clusters < 1) clusters = 1;
   cfg.gridDim = dim3(2 * clusters, 1, 1);
   e = cudaLaunchKernelEx(&cfg, kern, g.tmA, g.tmB, g.tmC, p);
   note_launch(1);
