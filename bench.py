@@ -222,8 +222,7 @@ def cast_gbs(dev="cuda", iters=20):
         es = x.element_size()
         for mode, bytes_per in (("tensor", 2 * es + 1), ("block1x128", es + 1 + 4 / 128), ("none", es + 1)):
             f = lambda: b2x.quantize(x, mode, torch.float8_e4m3fn)  # noqa: E731
-            f()
-            ms = timed(f, iters)
+            ms = graph_ms(f, iters)  # device time, no host launch gaps
             out[f"{src}_{mode}"] = round(n * bytes_per / (ms * 1e-3) / 1e9, 1)
     return out
 

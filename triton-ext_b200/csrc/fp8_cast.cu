@@ -49,7 +49,20 @@ __device__ __forceinline__ uint16_t cvt2(float lo, float hi) {
 // min and the sign bit of y is kept, so a NaN becomes +m or -m by its sign
 // bit.  Pinned by the golden vectors in tests/golden (recorded on a B200 from
 // a plain-Triton restatement of the recipe).
-__device__ __forceinline__ float clamp_sym(float y, float m) { return copysignf(fminf(fabsf(y), m), y); }
+// One instruction: min.xorsign.abs gives min(|y|, |m|) with the sign bit of
+// y XOR m (m > 0, so y's), and like min it returns the non-NaN operand.
+__device__ __forceinline__ float clamp_sym(float y, float m) {
+  float r;
+  asm("min.xorsign.abs.f32 %0, %1, %2;" : "=f"(r) : "f"(y), "f"(m));
+  return r;
+}
+// max(|a|, |b|) up to sign (the sign bit is a XOR b; callers take |result|
+// once at the end); NaN operands are ignored like fmaxf.
+__device__ __forceinline__ float absmax_xs(float a, float b) {
+  float r;
+  asm("max.xorsign.abs.f32 %0, %1, %2;" : "=f"(r) : "f"(a), "f"(b));
+  return r;
+}
 
 // Quantize values.  SCALED: multiply by inv first; the GPU's fp32 multiply
 // returns the canonical (positive) NaN for any NaN result, so after scaling
@@ -156,10 +169,11 @@ __device__ __forceinline__ uint2 quant8(const float (&v)[8], float inv) {
 }
 
 __device__ __forceinline__ float absmax8(const float (&v)[8]) {
-  float m = 0.f;
-#pragma unroll
-  for (int i = 0; i < 8; ++i) m = fmaxf(m, fabsf(v[i]));  // fmaxf ignores NaN
-  return m;
+  // pairwise tree of NaN-ignoring |max|; the sign bits are dropped at the end
+  float a = absmax_xs(v[0], v[1]), b = absmax_xs(v[2], v[3]);
+  float c = absmax_xs(v[4], v[5]), d = absmax_xs(v[6], v[7]);
+  // fmaxf(0, .) turns the all-NaN case into 0, as a NaN-ignoring max from 0 would
+  return fmaxf(0.f, fabsf(absmax_xs(absmax_xs(a, b), absmax_xs(c, d))));
 }
 
 struct CastGeom {
@@ -428,7 +442,7 @@ int cast_num_partials(int64_t nsegs, int num_sms) {
 template <typename T, int FP8>
 static cudaError_t launch_cast_t(const CastGeom& g, int mode, void* scale, int64_t ld_scale, uint32_t* partials,
                                  int num_sms, cudaStream_t st) {
-  constexpr int U = sizeof(T) == 4 ? 4 : 8;  // 128 B of loads in flight per lane either way
+  constexpr int U = 4;  // 4 x 8 elements per lane per step (128 B of fp32 / 64 B of bf16 in flight)
   switch (mode) {
     case B2X_SCALE_NONE:
     case B2X_SCALE_TENSOR_GIVEN:
@@ -447,14 +461,18 @@ static cudaError_t launch_cast_t(const CastGeom& g, int mode, void* scale, int64
       break;
     }
     case B2X_SCALE_BLOCK_1x128: {
-      auto k = quant_rowblock_kernel<T, FP8, 128, U>;
-      k<<<grid_for(g.nsegs, U, resident_ctas(k), num_sms), 256, 0, st>>>(g, scale, ld_scale);
+      // Row-block kernels do a shuffle reduction and two divisions per group:
+      // a shallower unroll keeps more warps resident to hide that latency.
+      constexpr int UR = sizeof(T) == 4 ? 4 : 4;
+      auto k = quant_rowblock_kernel<T, FP8, 128, UR>;
+      k<<<grid_for(g.nsegs, UR, resident_ctas(k), num_sms), 256, 0, st>>>(g, scale, ld_scale);
       note_launch(1);
       break;
     }
     case B2X_SCALE_MX_1x32: {
-      auto k = quant_rowblock_kernel<T, FP8, 32, U>;
-      k<<<grid_for(g.nsegs, U, resident_ctas(k), num_sms), 256, 0, st>>>(g, scale, ld_scale);
+      constexpr int UR = 4;
+      auto k = quant_rowblock_kernel<T, FP8, 32, UR>;
+      k<<<grid_for(g.nsegs, UR, resident_ctas(k), num_sms), 256, 0, st>>>(g, scale, ld_scale);
       note_launch(1);
       break;
     }
