@@ -376,8 +376,9 @@ def matmul(a, b, config=None, use_heuristic=False, *, scale_a: Optional[torch.Te
             cfg = dict(config)
             cfg.pop("ctas_per_cga", None)
             cfg.pop("pre_hook", None)
-            if mode == "block":
-                cfg["BLOCK_SIZE_N"], cfg["SPLIT_K"] = 128, 1
+            if mode == "block":  # 128 or 256 (paired CTAs) wide tiles; libb2x picks when unset
+                cfg["BLOCK_SIZE_N"] = cfg.get("BLOCK_SIZE_N", 0) if cfg.get("BLOCK_SIZE_N", 0) in (128, 256) else 0
+                cfg["SPLIT_K"] = 1
             fields = tuple(_to_b2x_config(cfg, K))
             if ckey is not None:
                 _config_cache[ckey] = fields

@@ -240,7 +240,11 @@ b2x_status b2x_gemm_default_config(const b2x_gemm_args* a, b2x_gemm_config* out)
   c.block_m = 128;
   c.block_k = 128;
   if (blockscaled) {
-    c.block_n = 128;  // B scales are per 128x128 tile: one scale per N tile and K block
+    // B scales are per 128x128 tile.  Paired CTAs take 256-wide tiles (two
+    // scale columns); a single CTA takes 128-wide tiles.
+    const bool bs_pair = a->M > 128 && c.num_ctas != 1;
+    c.block_n = bs_pair && c.block_n != 128 ? 256 : 128;
+    c.num_ctas = bs_pair ? 2 : 1;
     c.split_k = 1;
   }
   // M <= 64 with a K-major B runs the operand-swapped small-M kernel: 128
@@ -336,7 +340,7 @@ b2x_status b2x_gemm_default_config(const b2x_gemm_args* a, b2x_gemm_config* out)
   // Paired CTAs (256x256 tiles over two SMs) for large non-split problems:
   // a third less operand traffic per SM.  Needs 256-wide tiles and more
   // than one 128-row block of M.
-  const bool pair_ok = c.split_k == 1 && c.block_n == 256 && !blockscaled && a->M > 128;
+  const bool pair_ok = c.split_k == 1 && (c.block_n == 256 || blockscaled) && a->M > 128;
   if (c.num_ctas == 0) c.num_ctas = pair_ok ? 2 : 1;
   if (c.num_ctas == 2 && !pair_ok) c.num_ctas = 1;
   *out = c;
@@ -408,8 +412,9 @@ b2x_status b2x_fp8_gemm(const b2x_gemm_args* a, void* stream) {
     return fail(B2X_ERR_UNSUPPORTED, "b2x_fp8_gemm: BLOCK_SIZE_N must be 64, 128 or 256 (got %d)", c.block_n);
   if (b_mn && c.block_n < 128)
     return fail(B2X_ERR_UNSUPPORTED, "b2x_fp8_gemm: row-major B needs BLOCK_SIZE_N >= 128");
-  if (blockscaled && (c.block_n != 128 || c.split_k > 1))
-    return fail(B2X_ERR_UNSUPPORTED, "b2x_fp8_gemm: block-scaled GEMM runs with BLOCK_SIZE_N = 128, SPLIT_K = 1");
+  if (blockscaled && (c.split_k > 1 || (c.block_n != 128 && !(c.block_n == 256 && c.num_ctas == 2))))
+    return fail(B2X_ERR_UNSUPPORTED,
+                "b2x_fp8_gemm: block-scaled GEMM runs with SPLIT_K = 1 and 128-wide tiles (256 on CTA pairs)");
   const int k_tiles = ceil_div(a->K, 128);
   if (c.split_k < 1) return fail(B2X_ERR_INVALID_ARG, "b2x_fp8_gemm: SPLIT_K must be >= 1");
   if (c.split_k > 1) {
@@ -474,7 +479,8 @@ b2x_status b2x_fp8_gemm(const b2x_gemm_args* a, void* stream) {
                   128, 128, CU_TENSOR_MAP_SWIZZLE_128B, "B (row-major)");
   else
     s = encode_2d(&g.tmB, CU_TENSOR_MAP_DATA_TYPE_UINT8, a->b, (uint64_t)a->K, (uint64_t)a->N, (uint64_t)a->ldb_n,
-                  128, g.pair ? 128u : (uint32_t)c.block_n, CU_TENSOR_MAP_SWIZZLE_128B, "B (K-major)");
+                  128, g.pair ? (uint32_t)c.block_n / 2 : (uint32_t)c.block_n, CU_TENSOR_MAP_SWIZZLE_128B,
+                  "B (K-major)");
   if (s != B2X_OK) return s;
   s = encode_2d(&g.tmC, a->c_type == B2X_F16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16,
                 a->c, (uint64_t)a->N, (uint64_t)a->M, (uint64_t)a->ldc * 2, 64, 128, CU_TENSOR_MAP_SWIZZLE_128B, "C");
@@ -492,7 +498,8 @@ b2x_status b2x_fp8_gemm(const b2x_gemm_args* a, void* stream) {
   }
 
   if (blockscaled)
-    e = launch_fp8_gemm_blockscaled(g, (cudaStream_t)stream);
+    e = g.pair ? launch_fp8_gemm_blockscaled_pair(g, (cudaStream_t)stream)
+               : launch_fp8_gemm_blockscaled(g, (cudaStream_t)stream);
   else if (g.pair)
     e = launch_fp8_gemm_pair(g, (cudaStream_t)stream);
   else if (g.swap_ab)

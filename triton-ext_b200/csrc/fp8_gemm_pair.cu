@@ -224,7 +224,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           // the last conversion and store.
           tc_fence_before();
           named_bar_sync(bar_id, 128);
-          if (wg_tid == 0) mbar_arrive_cluster(tempty_leader);
+          if (wg_tid == 0) mbar_arrive_cluster_relaxed(tempty_leader);
         }
         uint32_t pk[32];
 #pragma unroll
