@@ -462,6 +462,10 @@ b2x_status b2x_fp8_gemm(const b2x_gemm_args* a, void* stream) {
     return v && v[0] == '1' ? 1 : 0;
   }();
   g.trace = trace_env;
+  // Both operands evict_last: measured best sustained (a streamed B marked
+  // evict_first or evict_normal re-reads more under the power cap).
+  g.l2_a = 0;
+  g.l2_b = 0;
   g.small_m = (!g.pair && !blockscaled && a->M <= 64) ? 1 : 0;
   g.swap_ab = (g.small_m && !b_mn && c.block_n == 128) ? 1 : 0;
   if (c.split_k > 1) {

@@ -43,6 +43,7 @@ struct GemmLaunch {
   int chunk3d;       // small_m with 3-D (x, row, K chunk) A/B tensor maps
   int swap_ab;       // small_m with K-major B: weights on the MMA's M side
   int trace;         // B2X_TRACE=1: per-CTA wait cycles into g_trace
+  int l2_a, l2_b;    // L2 eviction policy per operand (0 last, 1 normal, 2 first)
 };
 
 cudaError_t launch_fp8_gemm(const GemmLaunch& g, cudaStream_t st);

@@ -28,7 +28,12 @@ struct GemmParams {
   int64_t ldc;
   int chunk3d;      // small-M kernel: A and B maps are 3-D (x, row, K chunk)
   int trace;        // record per-CTA wait cycles in g_trace
+  int l2_a, l2_b;   // L2 policy per operand: 0 evict_last, 1 evict_normal, 2 evict_first
 };
+
+__device__ __forceinline__ uint64_t l2_policy(int which) {
+  return which == 2 ? policy_evict_first() : (which == 1 ? policy_evict_normal() : policy_evict_last());
+}
 
 // Grouped tile order, the same mapping as _compute_pid (blackwell_gemm_ws.py:433-439).
 __device__ __forceinline__ void compute_pid(int tile, int num_pid_in_group, int num_pid_m, int group_size_m,

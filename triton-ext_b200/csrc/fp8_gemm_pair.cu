@@ -105,7 +105,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (warp == 0) {
     // ------------------------------------------------------------ producer
     if (lane == 0) {
-      const uint64_t pol = policy_evict_last();
+      const uint64_t pol_a = l2_policy(p.l2_a);
+      const uint64_t pol_b = l2_policy(p.l2_b);
       int stage = 0;
       uint32_t phase = 0, issued_mask = 0;
       uint32_t pend_phase[STAGES];
@@ -124,11 +125,11 @@ __global__ void __launch_bounds__(kThreads, 1)
           if (leader) mbar_arrive_expect_tx(&full[stage], 2 * L::kStageBytes);
           uint8_t* sA = smem + L::kAOff + stage * L::kABytes;
           uint8_t* sB = smem + L::kBOff + stage * L::kBBytes;
-          tma_load_2d_pair(sA, &tmA, full_leader, kb * kBK, row0, pol);
+          tma_load_2d_pair(sA, &tmA, full_leader, kb * kBK, row0, pol_a);
           if (B_MN)
-            tma_load_2d_pair(sB, &tmB, full_leader, col0, kb * kBK, pol);
+            tma_load_2d_pair(sB, &tmB, full_leader, col0, kb * kBK, pol_b);
           else
-            tma_load_2d_pair(sB, &tmB, full_leader, kb * kBK, col0, pol);
+            tma_load_2d_pair(sB, &tmB, full_leader, kb * kBK, col0, pol_b);
           issued_mask |= 1u << stage;
           pend_phase[stage] = phase;
           if (++stage == STAGES) {
@@ -320,6 +321,8 @@ cudaError_t launch_fp8_gemm_pair(const GemmLaunch& g, cudaStream_t st) {
   p.scale_b = g.scale_b;
   p.c = g.c;
   p.ldc = g.ldc;
+  p.l2_a = g.l2_a;
+  p.l2_b = g.l2_b;
   return g.b_mn ? launch_pair_t<S, 1>(g, p, st) : launch_pair_t<S, 0>(g, p, st);
 }
 
