@@ -297,6 +297,9 @@ def main():
     ap.add_argument("--workload", default="llama", choices=["llama", "gemm", "cast", "decode", "blockscaled"])
     ap.add_argument("--shape", default="8192,8192,8192")
     ap.add_argument("--no-side", action="store_true", help="skip the side measurements")
+    ap.add_argument("--comm", default="fused", choices=["fused", "nccl"],
+                    help="N>1: down GEMM with its all-reduce fused in-kernel, or followed by NCCL all-reduce")
+    ap.add_argument("--fused-mode", default="auto", choices=["auto", "multicast", "peer"])
     args = ap.parse_args()
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -330,7 +333,7 @@ def main():
 
     peaks = load_peaks()
     from b2x.sharded import LlamaFP8LinearSet
-    ls = LlamaFP8LinearSet(rank, world, dev)
+    ls = LlamaFP8LinearSet(rank, world, dev, comm=args.comm, fused_mode=args.fused_mode)
     for _ in range(max(args.warmup, 3)):
         ls.step()
     torch.cuda.synchronize()
@@ -429,7 +432,10 @@ def main():
             "vs_baseline": None, "dtype": "e4m3", "data": "synthetic (seeded ~N(0,1), per-tensor amax/448 e4m3)",
             "config": {"workload": "llama3-70b fp8 linear set @ 8192 tokens: qkv 8192x10240x8192, "
                                    "gate_up 8192x57344x8192, down 8192x8192x28672",
-                       "parallelism": f"qkv/gate_up N-sharded, down K-sharded + all-reduce (x{world})",
+                       "parallelism": (f"qkv/gate_up N-sharded, down K-sharded + all-reduce (x{world}); "
+                                       + (f"all-reduce fused into the down GEMM ({ls.fused.mode})" if ls.fused
+                                          else ("NCCL all-reduce overlapped on a side stream" if world > 1
+                                                else "single GPU"))),
                        "l2": "inputs larger than L2 (1.2 GB of fp8 operands per step)",
                        "tflops_per_gpu": value / world},
             "roofline": {"bound": "tensor", "kernel": "fp8_gemm_pair_kernel (gate+up launch)",

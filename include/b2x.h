@@ -206,6 +206,45 @@ B2X_API b2x_status b2x_splitk_reduce(const void* ws, b2x_dtype ws_type, void* c,
  */
 B2X_API b2x_status b2x_fp8_gemm_splitk_noalloc(const b2x_gemm_args* args, void* stream);
 
+/* ------------------------------------------------------------ GEMM + all-reduce */
+
+/*
+ * Row-parallel fp8 GEMM fused with the sum over the GPUs of one node:
+ *   C = sum over ranks r of ( A_r . B_r * scales_r ),  bf16 [M, N] on every rank,
+ * where each rank passes its own K-slice A_r [M, K/world] and B_r.  The ranks'
+ * partial tiles are summed while the GEMM runs (each 128 x 256 output unit is
+ * reduced by the last rank to finish it, through NVSwitch multicast or peer
+ * loads/stores over NVLink), so no separate collective follows.
+ *
+ * The GEMM arguments are those of b2x_fp8_gemm with these limits: scale mode
+ * NONE / TENSOR / TENSOR_GIVEN, K-major B, bf16 C, M and N multiples of 256,
+ * ldc a multiple of 8.  `args->c` must be this rank's copy of a buffer every
+ * rank can reach (c_peers[rank]); the result overwrites it on every rank.
+ * The signal buffer (b2x_allreduce_signal_words 32-bit words per rank, all
+ * zero before the first call) carries the arrival and completion counts.
+ * Every rank must make the same sequence of calls (same shapes, same
+ * buffers), passing epoch = 1 on the first call after zeroing the signal
+ * buffer and one more on each later call.  The kernel ends when the sum is
+ * complete on this rank; a peer that never takes part makes it give up after
+ * 10 s with B2X_ERR_TIMEOUT recorded in the device status word, after which
+ * the signal buffers must be zeroed on every rank before the next call.
+ * No counterpart in the reference, which has no multi-GPU code path; it
+ * replaces, for the tensor-parallel layer set, a GEMM followed by an NCCL
+ * all-reduce of its output.
+ */
+#define B2X_AR_MAX_RANKS 8
+typedef struct {
+  int rank, world;                      /* 1 <= world <= B2X_AR_MAX_RANKS */
+  void* c_multicast;                    /* multicast address of C's buffer, or NULL for peer mode */
+  void* c_peers[B2X_AR_MAX_RANKS];      /* C's buffer on each rank, as mapped in this process */
+  void* signal_multicast;               /* multicast address of the signal buffer (with c_multicast) */
+  void* signal_peers[B2X_AR_MAX_RANKS]; /* the signal buffer on each rank */
+  uint32_t epoch;                       /* 1, 2, 3, ... per call */
+} b2x_allreduce_args;
+
+B2X_API size_t b2x_allreduce_signal_words(int64_t M, int64_t N);
+B2X_API b2x_status b2x_fp8_gemm_allreduce(const b2x_gemm_args* args, const b2x_allreduce_args* ar, void* stream);
+
 /* ------------------------------------------------------------------ misc */
 
 /* Message for the calling thread's last failed call ("" if none). */

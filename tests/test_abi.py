@@ -52,14 +52,16 @@ def test_struct_layouts_match_header():
     if cc is None:
         pytest.skip("no C compiler")
     src = '#include <stdio.h>\n#include "b2x.h"\nint main(){printf("%zu %zu %zu\\n", sizeof(b2x_cast_args),' \
-          ' sizeof(b2x_gemm_config), sizeof(b2x_gemm_args)); return 0;}\n'
+          ' sizeof(b2x_gemm_config), sizeof(b2x_gemm_args)); printf("%zu\\n", sizeof(b2x_allreduce_args));' \
+          ' return 0;}\n'
     with tempfile.TemporaryDirectory() as d:
         with open(os.path.join(d, "p.c"), "w") as f:
             f.write(src)
         exe = os.path.join(d, "p")
         subprocess.run([cc, "-I", os.path.join(ROOT, "include"), os.path.join(d, "p.c"), "-o", exe], check=True)
         sizes = [int(v) for v in subprocess.run([exe], capture_output=True, text=True, check=True).stdout.split()]
-    assert sizes == [ctypes.sizeof(L.CastArgs), ctypes.sizeof(L.GemmConfig), ctypes.sizeof(L.GemmArgs)]
+    assert sizes == [ctypes.sizeof(L.CastArgs), ctypes.sizeof(L.GemmConfig), ctypes.sizeof(L.GemmArgs),
+                     ctypes.sizeof(L.AllReduceArgs)]
 
 
 def _gemm_args(**kw):
@@ -116,6 +118,47 @@ def test_block_scaled_requires_kmajor_b():
     L = _lib()
     g = _gemm_args(ldb_k=256, ldb_n=1, scale_mode=L.SCALE_BLOCK_1x128, scale_a=0x40000, scale_b=0x50000)
     assert L.lib().b2x_fp8_gemm(ctypes.byref(g), None) == L.ERR_UNSUPPORTED
+
+
+def _ar_args(**kw):
+    L = _lib()
+    r = L.AllReduceArgs()
+    r.rank, r.world, r.epoch = 0, 2, 1
+    r.c_peers[0], r.c_peers[1] = 0x30000, 0x70000
+    r.signal_peers[0], r.signal_peers[1] = 0x90000, 0xA0000
+    for k, v in kw.items():
+        setattr(r, k, v)
+    return r
+
+
+def test_allreduce_signal_words():
+    lib = _lib().lib()
+    assert lib.b2x_allreduce_signal_words(8192, 8192) == 64 + 64 * 32
+    assert lib.b2x_allreduce_signal_words(256, 256) == 64 + 2
+
+
+@pytest.mark.parametrize("gemm_kw,ar_kw,status", [
+    ({}, {"world": 9}, "ERR_INVALID_ARG"),
+    ({}, {"rank": 2}, "ERR_INVALID_ARG"),
+    ({}, {"epoch": 0}, "ERR_INVALID_ARG"),
+    ({"M": 384}, {}, "ERR_UNSUPPORTED"),                      # M not a multiple of 256
+    ({"c_type": 2}, {}, "ERR_UNSUPPORTED"),                   # fp16 output
+    ({"ldb_k": 256, "ldb_n": 1}, {}, "ERR_UNSUPPORTED"),      # row-major B
+    ({"c": 0x50000}, {}, "ERR_INVALID_ARG"),                  # C is not this rank's buffer
+    ({}, {"c_multicast": 0x100000}, "ERR_INVALID_ARG"),      # multicast C without multicast signals
+    ({}, {"signal_peers": None}, "ERR_INVALID_ARG"),
+])
+def test_fused_allreduce_rejects_bad_arguments(gemm_kw, ar_kw, status):
+    L = _lib()
+    g = _gemm_args(**gemm_kw)
+    if ar_kw.get("signal_peers", 1) is None:
+        r = _ar_args()
+        r.signal_peers[1] = 0
+    else:
+        r = _ar_args(**ar_kw)
+    st = L.lib().b2x_fp8_gemm_allreduce(ctypes.byref(g), ctypes.byref(r), None)
+    assert st == getattr(L, status), L.lib().b2x_last_error()
+    assert L.lib().b2x_last_error()
 
 
 def _cast_args(**kw):

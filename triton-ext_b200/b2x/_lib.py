@@ -26,8 +26,10 @@ EXPORTED = (
     "b2x_cast_workspace_size", "b2x_fp8_cast", "b2x_amax", "b2x_gemm_default_config",
     "b2x_gemm_workspace_size", "b2x_fp8_gemm", "b2x_splitk_reduce", "b2x_last_error",
     "b2x_read_device_status", "b2x_abi_version", "b2x_launch_count", "b2x_fp8_gemm_splitk_noalloc",
-    "b2x_trace_read",
+    "b2x_trace_read", "b2x_allreduce_signal_words", "b2x_fp8_gemm_allreduce",
 )
+
+AR_MAX_RANKS = 8
 
 
 class CastArgs(ctypes.Structure):
@@ -57,6 +59,15 @@ class GemmArgs(ctypes.Structure):
         ("scale_b", ctypes.c_void_p), ("sb_stride_k", ctypes.c_int64), ("sb_stride_n", ctypes.c_int64),
         ("workspace", ctypes.c_void_p), ("workspace_bytes", ctypes.c_size_t),
         ("config", GemmConfig),
+    ]
+
+
+class AllReduceArgs(ctypes.Structure):
+    _fields_ = [
+        ("rank", ctypes.c_int), ("world", ctypes.c_int),
+        ("c_multicast", ctypes.c_void_p), ("c_peers", ctypes.c_void_p * AR_MAX_RANKS),
+        ("signal_multicast", ctypes.c_void_p), ("signal_peers", ctypes.c_void_p * AR_MAX_RANKS),
+        ("epoch", ctypes.c_uint32),
     ]
 
 
@@ -106,6 +117,10 @@ def lib() -> ctypes.CDLL:
         L.b2x_fp8_gemm.restype = ctypes.c_int
         L.b2x_trace_read.argtypes = [ctypes.c_void_p, ctypes.c_int, ctypes.POINTER(ctypes.c_int)]
         L.b2x_trace_read.restype = ctypes.c_int
+        L.b2x_allreduce_signal_words.argtypes = [ctypes.c_int64, ctypes.c_int64]
+        L.b2x_allreduce_signal_words.restype = ctypes.c_size_t
+        L.b2x_fp8_gemm_allreduce.argtypes = [ctypes.POINTER(GemmArgs), ctypes.POINTER(AllReduceArgs), ctypes.c_void_p]
+        L.b2x_fp8_gemm_allreduce.restype = ctypes.c_int
         L.b2x_fp8_gemm_splitk_noalloc.argtypes = [ctypes.POINTER(GemmArgs), ctypes.c_void_p]
         L.b2x_fp8_gemm_splitk_noalloc.restype = ctypes.c_int
         L.b2x_splitk_reduce.argtypes = [ctypes.c_void_p, ctypes.c_int, ctypes.c_void_p, ctypes.c_int,

@@ -10,8 +10,11 @@ projections are:
   K-sharding the down projection consumes);
 * row-parallel (down): each rank holds columns [r*K/g, (r+1)*K/g) of the
   [N, K] weight and the matching K-slice of the input, computes a partial
-  [M, N] output and the partials are summed with an all-reduce over NCCL
-  (NVLink / NVSwitch).
+  [M, N] output and the partials are summed over the group.  On GPUs the sum
+  is fused into the GEMM kernel (FusedRowParallel: every 128 x 256 output
+  unit is reduced over NVSwitch multicast or NVLink peer memory as soon as
+  the last rank has stored it); `row_parallel` with an NCCL all-reduce after
+  the GEMM is the unfused form.
 
 The GEMM is injectable (`mm`) so the partitioning logic can be checked on
 CPU ranks (gloo) against an unsharded product.
@@ -66,21 +69,102 @@ def row_parallel(a_shard, sa, w_shard, sw, group=None, mm: Callable = _default_m
     return (part, None) if async_op else part
 
 
+class FusedRowParallel:
+    """Row-parallel fp8 GEMM with the all-reduce of its output inside the GEMM
+    kernel (include/b2x.h, b2x_fp8_gemm_allreduce).
+
+    Owns, per process group and output shape, a bf16 [M, N] output buffer and
+    a small signal buffer in symmetric memory (every rank maps every rank's
+    copy; with NVSwitch multicast support one multicast address covers all
+    copies).  Each call returns the output buffer itself: the next call
+    overwrites it.  All ranks must make the same calls in the same order.
+
+    mode: "auto" (multicast when the group supports it, else peer loads and
+    stores), "multicast" or "peer".
+    """
+
+    def __init__(self, M: int, N: int, device, group=None, mode: str = "auto"):
+        import torch.distributed._symmetric_memory as symm_mem
+        from . import _lib as L
+        self.M, self.N = M, N
+        self.device = torch.device(device)
+        self.group = group if group is not None else dist.group.WORLD
+        self.world = dist.get_world_size(self.group)
+        self.rank = dist.get_rank(self.group)
+        if self.world > L.AR_MAX_RANKS:
+            raise ValueError(f"fused all-reduce supports at most {L.AR_MAX_RANKS} ranks, got {self.world}")
+        words = int(L.lib().b2x_allreduce_signal_words(M, N))
+        self.out = symm_mem.empty((M, N), dtype=torch.bfloat16, device=self.device)
+        self.signal = symm_mem.empty((words,), dtype=torch.int32, device=self.device)
+        self.signal.zero_()
+        name = self.group.group_name
+        h_out = symm_mem.rendezvous(self.out, name)
+        h_sig = symm_mem.rendezvous(self.signal, name)
+        use_mc = mode == "multicast" or (mode == "auto" and bool(h_out.has_multicast_support)
+                                         and bool(h_sig.has_multicast_support))
+        if mode not in ("auto", "multicast", "peer"):
+            raise ValueError(f"mode must be auto, multicast or peer, got {mode!r}")
+        if use_mc and not (h_out.multicast_ptr and h_sig.multicast_ptr):
+            raise RuntimeError("NVSwitch multicast is not available for this group")
+        self.mode = "multicast" if use_mc else "peer"
+        ar = L.AllReduceArgs()
+        ar.rank, ar.world = self.rank, self.world
+        off_c = self.out.data_ptr() - h_out.buffer_ptrs[self.rank]
+        off_s = self.signal.data_ptr() - h_sig.buffer_ptrs[self.rank]
+        for r in range(self.world):
+            ar.c_peers[r] = h_out.buffer_ptrs[r] + off_c
+            ar.signal_peers[r] = h_sig.buffer_ptrs[r] + off_s
+        if use_mc:
+            ar.c_multicast = h_out.multicast_ptr + off_c
+            ar.signal_multicast = h_sig.multicast_ptr + off_s
+        self._ar = ar
+        self._handles = (h_out, h_sig)
+        self.epoch = 0
+        torch.cuda.synchronize(self.device)
+        dist.barrier(self.group)  # every rank's signal buffer is zero before any kernel runs
+
+    def __call__(self, a_shard: torch.Tensor, sa: Optional[torch.Tensor], w_shard: torch.Tensor,
+                 sw: Optional[torch.Tensor], cfg: Optional[dict] = None) -> torch.Tensor:
+        """sum over ranks of a_shard [M, K/g] . w_shard [N, K/g]^T (fp8, per-tensor
+        scales or none) into the shared bf16 [M, N] buffer, which is returned."""
+        import ctypes
+        from . import _lib as L
+        from . import ops
+        from .blackwell_gemm_ws import _to_b2x_config
+        if a_shard.shape[0] != self.M or w_shard.shape[0] != self.N:
+            raise ValueError(f"shapes {tuple(a_shard.shape)} x {tuple(w_shard.shape)} do not match this "
+                             f"[{self.M}, {self.N}] buffer")
+        mode = "none" if sa is None else "tensor"
+        fields = tuple(_to_b2x_config(cfg or {}, a_shard.shape[1]))
+        g = ops._gemm_args(a_shard, w_shard.t(), self.out, mode, sa, sw, fields)
+        self.epoch += 1
+        self._ar.epoch = self.epoch & 0xFFFFFFFF or 1
+        with torch.cuda.device(self.device):
+            st = L.lib().b2x_fp8_gemm_allreduce(ctypes.byref(g), ctypes.byref(self._ar),
+                                                ctypes.c_void_p(torch.cuda.current_stream(self.device).cuda_stream))
+        L.check(st)
+        return self.out
+
+
 class LlamaFP8LinearSet:
     """The Llama-3-70B-shaped fp8 linear set of one transformer block at a
     fixed token count, sharded over the process group: QKV and gate+up
     column-parallel, down row-parallel + all-reduce.
 
-    step() order on N > 1 ranks: down first, its all-reduce issued on a side
-    stream, then QKV and gate+up on the compute stream while the all-reduce
-    runs (GEMMs are launched with NUM_SMS = all but `comm_sms` SMs so NCCL's
-    kernels find free SMs).
+    comm = "fused" (default on GPUs): the down projection and the sum of its
+    partials over the group are one kernel (FusedRowParallel), followed by
+    QKV and gate+up on all SMs.
+    comm = "nccl": down first, its NCCL all-reduce issued on a side stream,
+    then QKV and gate+up on the compute stream while the all-reduce runs
+    (launched with NUM_SMS = all but `comm_sms` SMs so NCCL's kernels find
+    free SMs).
     """
 
     SHAPES = {"qkv": (8192, 10240, 8192), "gate_up": (8192, 57344, 8192), "down": (8192, 8192, 28672)}
 
     def __init__(self, rank: int, world: int, device, tokens: int = 8192, seed: int = 1234, comm_sms: int = 16,
-                 mm: Callable = _default_mm, make_input: Optional[Callable] = None):
+                 mm: Callable = _default_mm, make_input: Optional[Callable] = None, comm: str = "fused",
+                 fused_mode: str = "auto"):
         self.rank, self.world, self.device, self.mm = rank, world, device, mm
         self.tokens = tokens
         M = tokens
@@ -97,13 +181,27 @@ class LlamaFP8LinearSet:
         self.a2, self.sa2 = make((M, kd), g, device)
         self.wd, self.sd = make((nd, kd), g, device)
         self.flops_total = sum(2.0 * (M / 8192) * m * n * k for (m, n, k) in self.SHAPES.values())
-        self.comm_stream = torch.cuda.Stream(device) if (world > 1 and torch.device(device).type == "cuda") else None
+        on_gpu = world > 1 and torch.device(device).type == "cuda"
+        if comm not in ("fused", "nccl"):
+            raise ValueError(f"comm must be 'fused' or 'nccl', got {comm!r}")
+        self.comm = comm if on_gpu else "nccl"
+        self.fused = FusedRowParallel(M, nd, device, mode=fused_mode) if self.comm == "fused" else None
+        self.comm_stream = torch.cuda.Stream(device) if (on_gpu and self.comm == "nccl") else None
         n_sms = torch.cuda.get_device_properties(device).multi_processor_count if self.comm_stream else 0
         self.overlap_cfg = {"NUM_SMS": n_sms - comm_sms} if self.comm_stream else {}
         self.cfg = {}
 
     def step(self, events=None):
         """One pass over the set; returns (qkv_out, gate_up_out, down_out)."""
+        if self.fused is not None:
+            d = self.fused(self.a2, self.sa2, self.wd, self.sd)
+            q = self.mm(self.x, self.wq, self.sx, self.sq, self.cfg)
+            if events:
+                events[0].record()
+            gu = self.mm(self.x, self.wgu, self.sx, self.sgu, self.cfg)
+            if events:
+                events[1].record()
+            return q, gu, d
         if self.world > 1 and self.comm_stream is not None:
             d = self.mm(self.a2, self.wd, self.sa2, self.sd, self.cfg)
             ready = torch.cuda.Event()

@@ -356,8 +356,9 @@ size_t b2x_gemm_workspace_size(const b2x_gemm_args* a) {
   return (size_t)(align_up((uint64_t)a->M * a->N * 4, 256) + align_up(tiles * 4, 256));
 }
 
-b2x_status b2x_fp8_gemm(const b2x_gemm_args* a, void* stream) {
-  t_err[0] = 0;
+// The GEMM behind b2x_fp8_gemm and b2x_fp8_gemm_allreduce (ar != NULL: the
+// paired kernel with the fused all-reduce epilogue).
+static b2x_status fp8_gemm_impl(const b2x_gemm_args* a, const ArParams* ar, void* stream) {
   if (!a) return fail(B2X_ERR_INVALID_ARG, "b2x_fp8_gemm: args is NULL");
   if (!is_fp8(a->a_type) || !is_fp8(a->b_type))
     return fail(B2X_ERR_UNSUPPORTED, "b2x_fp8_gemm: A and B must be e4m3 or e5m2 (got %d, %d)", (int)a->a_type,
@@ -365,7 +366,7 @@ b2x_status b2x_fp8_gemm(const b2x_gemm_args* a, void* stream) {
   if (a->c_type != B2X_BF16 && a->c_type != B2X_F16)
     return fail(B2X_ERR_UNSUPPORTED, "b2x_fp8_gemm: C must be bf16 or fp16 (got %d)", (int)a->c_type);
   if (a->M < 0 || a->N < 0 || a->K < 0) return fail(B2X_ERR_INVALID_ARG, "b2x_fp8_gemm: negative shape");
-  if (a->M == 0 || a->N == 0) return B2X_OK;
+  if ((a->M == 0 || a->N == 0) && !ar) return B2X_OK;
   if (a->K == 0) return fail(B2X_ERR_UNSUPPORTED, "b2x_fp8_gemm: K == 0 (C would be all zero)");
   if (a->M >= (1LL << 31) || a->N >= (1LL << 31) || a->K >= (1LL << 31))
     return fail(B2X_ERR_UNSUPPORTED, "b2x_fp8_gemm: dimensions must be < 2^31");
@@ -501,6 +502,11 @@ b2x_status b2x_fp8_gemm(const b2x_gemm_args* a, void* stream) {
     }
   }
 
+  if (ar) {
+    if (!g.pair || blockscaled || c.split_k != 1 || c.block_n != 256 || b_mn)
+      return fail(B2X_ERR_UNSUPPORTED, "b2x_fp8_gemm_allreduce: this shape does not run on the paired kernel");
+    g.ar = *ar;
+  }
   if (blockscaled)
     e = g.pair ? launch_fp8_gemm_blockscaled_pair(g, (cudaStream_t)stream)
                : launch_fp8_gemm_blockscaled(g, (cudaStream_t)stream);
@@ -512,6 +518,66 @@ b2x_status b2x_fp8_gemm(const b2x_gemm_args* a, void* stream) {
     e = launch_fp8_gemm(g, (cudaStream_t)stream);
   if (e != cudaSuccess) return cuda_fail(e, "b2x_fp8_gemm launch");
   return B2X_OK;
+}
+
+b2x_status b2x_fp8_gemm(const b2x_gemm_args* a, void* stream) {
+  t_err[0] = 0;
+  return fp8_gemm_impl(a, nullptr, stream);
+}
+
+size_t b2x_allreduce_signal_words(int64_t M, int64_t N) {
+  if (M <= 0 || N <= 0) return (size_t)kArArrive0;
+  return (size_t)kArArrive0 + (size_t)((M + 127) / 128) * (size_t)((N + 255) / 256);
+}
+
+b2x_status b2x_fp8_gemm_allreduce(const b2x_gemm_args* args, const b2x_allreduce_args* r, void* stream) {
+  t_err[0] = 0;
+  if (!args || !r) return fail(B2X_ERR_INVALID_ARG, "b2x_fp8_gemm_allreduce: NULL argument");
+  if (r->world < 1 || r->world > B2X_AR_MAX_RANKS || r->rank < 0 || r->rank >= r->world)
+    return fail(B2X_ERR_INVALID_ARG, "b2x_fp8_gemm_allreduce: rank %d / world %d out of range", r->rank, r->world);
+  if (args->c_type != B2X_BF16)
+    return fail(B2X_ERR_UNSUPPORTED, "b2x_fp8_gemm_allreduce: C must be bf16");
+  if (args->scale_mode == B2X_SCALE_BLOCK_1x128)
+    return fail(B2X_ERR_UNSUPPORTED, "b2x_fp8_gemm_allreduce: block-scaled operands are not supported");
+  if (args->M <= 0 || args->N <= 0 || (args->M % 256) || (args->N % 256))
+    return fail(B2X_ERR_UNSUPPORTED, "b2x_fp8_gemm_allreduce: M and N must be positive multiples of 256 (got %lld, %lld)",
+                (long long)args->M, (long long)args->N);
+  if (!(args->ldb_k == 1 && args->ldb_n >= args->K))
+    return fail(B2X_ERR_UNSUPPORTED, "b2x_fp8_gemm_allreduce: B must be K-major (an nn.Linear weight viewed as w.t())");
+  if (args->config.split_k > 1 || args->config.num_ctas == 1 || (args->config.block_n && args->config.block_n != 256))
+    return fail(B2X_ERR_UNSUPPORTED, "b2x_fp8_gemm_allreduce: runs on CTA pairs with 256-wide tiles and SPLIT_K = 1");
+  if (r->c_peers[r->rank] != args->c)
+    return fail(B2X_ERR_INVALID_ARG, "b2x_fp8_gemm_allreduce: args->c must be c_peers[rank]");
+  const bool mc = r->c_multicast != nullptr;
+  if (mc != (r->signal_multicast != nullptr))
+    return fail(B2X_ERR_INVALID_ARG, "b2x_fp8_gemm_allreduce: give both multicast addresses or neither");
+  for (int i = 0; i < r->world; ++i) {
+    if (!r->signal_peers[i] || ((uintptr_t)r->signal_peers[i] % 16))
+      return fail(B2X_ERR_INVALID_ARG, "b2x_fp8_gemm_allreduce: signal_peers[%d] missing or not 16-byte aligned", i);
+    if (!mc && (!r->c_peers[i] || ((uintptr_t)r->c_peers[i] % 16)))
+      return fail(B2X_ERR_INVALID_ARG, "b2x_fp8_gemm_allreduce: c_peers[%d] missing or not 16-byte aligned", i);
+  }
+  if (mc && (((uintptr_t)r->c_multicast % 16) || ((uintptr_t)r->signal_multicast % 16)))
+    return fail(B2X_ERR_INVALID_ARG, "b2x_fp8_gemm_allreduce: multicast addresses must be 16-byte aligned");
+  if (r->epoch == 0) return fail(B2X_ERR_INVALID_ARG, "b2x_fp8_gemm_allreduce: epoch starts at 1");
+  ArParams ar;
+  memset(&ar, 0, sizeof(ar));
+  ar.mode = mc ? 1 : 2;
+  ar.rank = r->rank;
+  ar.world = r->world;
+  ar.c_mc = reinterpret_cast<uint8_t*>(r->c_multicast);
+  ar.sig_mc = reinterpret_cast<uint32_t*>(r->signal_multicast);
+  for (int i = 0; i < r->world; ++i) {
+    ar.c_peer[i] = reinterpret_cast<uint8_t*>(r->c_peers[i]);
+    ar.sig_peer[i] = reinterpret_cast<uint32_t*>(r->signal_peers[i]);
+  }
+  const uint32_t units = (uint32_t)(b2x_allreduce_signal_words(args->M, args->N) - kArArrive0);
+  ar.done_target = r->epoch * units;  // wraps modulo 2^32, compared as a difference
+  b2x_gemm_args a = *args;
+  a.config.block_n = 256;
+  a.config.num_ctas = 2;
+  a.config.split_k = 1;
+  return fp8_gemm_impl(&a, &ar, stream);
 }
 
 b2x_status b2x_trace_read(uint64_t* out, int max_ctas, int* n_ctas) {

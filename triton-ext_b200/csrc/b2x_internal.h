@@ -22,6 +22,23 @@ int cast_num_partials(int64_t nsegs, int num_sms);
 cudaError_t launch_amax(const void* x, b2x_dtype xt, int64_t rows, int64_t cols, int64_t ld_x, float* out,
                         uint32_t* partials, int num_sms, cudaStream_t st);
 
+// Fused all-reduce of the GEMM output over the GPUs of one node
+// (b2x_fp8_gemm_allreduce).  Signal buffer layout, in 32-bit words on every
+// rank: word 0 counts finished reductions (done), words
+// [kArArrive0, kArArrive0 + units) count, per 128 x 256 output unit, the ranks
+// whose partial has landed (kept on rank unit % world).
+constexpr int kArMaxRanks = 8;
+constexpr int kArArrive0 = 64;
+struct ArParams {
+  int mode;                        // 0 off, 1 NVSwitch multicast, 2 peer loads/stores
+  int rank, world;
+  uint8_t* c_mc;                   // multicast address of C (mode 1)
+  uint8_t* c_peer[kArMaxRanks];    // C on every rank (mode 2)
+  uint32_t* sig_peer[kArMaxRanks]; // signal buffer on every rank
+  uint32_t* sig_mc;                // multicast address of the signal buffer (mode 1)
+  uint32_t done_target;            // value of the done word once this call is complete
+};
+
 struct GemmLaunch {
   CUtensorMap tmA, tmB, tmC;
   int64_t M, N, K;
@@ -44,6 +61,7 @@ struct GemmLaunch {
   int swap_ab;       // small_m with K-major B: weights on the MMA's M side
   int trace;         // B2X_TRACE=1: per-CTA wait cycles into g_trace
   int l2_a, l2_b;    // L2 eviction policy per operand (0 last, 1 normal, 2 first)
+  ArParams ar;       // fused all-reduce (pair kernel only)
 };
 
 cudaError_t launch_fp8_gemm(const GemmLaunch& g, cudaStream_t st);

@@ -35,6 +35,7 @@ enum : int {
   kStatusTimeoutMma = 0x102,
   kStatusTimeoutEpilogue = 0x103,
   kStatusTimeoutSplitK = 0x104,
+  kStatusTimeoutAllReduce = 0x105,  // a peer GPU never finished its share of a fused all-reduce
 };
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
@@ -384,6 +385,71 @@ __device__ __forceinline__ void red_add_f32(float* p, float a) {
 __device__ __forceinline__ void red_add_v4(float* p, float a, float b, float c, float d) {
   asm volatile("red.global.add.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(p), "f"(a), "f"(b), "f"(c), "f"(d)
                : "memory");
+}
+
+// ---------------------------------------------------------------- cross-GPU (NVLink / NVSwitch)
+// Peer pointers are another GPU's memory mapped into this process; multicast
+// pointers address the same offset on every GPU of an NVLink multicast group
+// (the NVSwitch replicates stores and reduces loads).  Only plain loads,
+// stores, atomics and multimem operations touch such memory here; no TMA
+// load ever reads it.
+
+// Make this thread's earlier async-proxy (TMA) global writes and generic
+// writes visible at system scope before a following release.
+__device__ __forceinline__ void fence_proxy_async_global() {
+  asm volatile("fence.proxy.async.global;" ::: "memory");
+}
+__device__ __forceinline__ void fence_acq_rel_sys() { asm volatile("fence.acq_rel.sys;" ::: "memory"); }
+
+__device__ __forceinline__ uint32_t atom_add_acq_rel_sys(uint32_t* p, uint32_t v) {
+  uint32_t old;
+  asm volatile("atom.add.acq_rel.sys.global.u32 %0, [%1], %2;" : "=r"(old) : "l"(p), "r"(v) : "memory");
+  return old;
+}
+__device__ __forceinline__ void red_add_release_sys(uint32_t* p, uint32_t v) {
+  asm volatile("red.add.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ void st_relaxed_sys(uint32_t* p, uint32_t v) {
+  asm volatile("st.relaxed.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
+  uint32_t v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+// Adds v to the word at this multicast address on every GPU of the group.
+__device__ __forceinline__ void multimem_red_add_release_sys(uint32_t* mc, uint32_t v) {
+  asm volatile("multimem.red.release.sys.global.add.u32 [%0], %1;" ::"l"(mc), "r"(v) : "memory");
+}
+// Sum over the group of eight bf16 values (16 bytes) at this multicast
+// address, accumulated in fp32 by the switch and returned as bf16.
+__device__ __forceinline__ uint4 multimem_ld_reduce_bf16x8(const void* mc) {
+  uint4 r;
+  asm volatile("multimem.ld_reduce.relaxed.sys.global.add.acc::f32.v4.bf16x2 {%0, %1, %2, %3}, [%4];"
+               : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
+               : "l"(mc)
+               : "memory");
+  return r;
+}
+// Stores 16 bytes at this multicast address on every GPU of the group.
+__device__ __forceinline__ void multimem_st_16(void* mc, uint4 v) {
+  asm volatile("multimem.st.relaxed.sys.global.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(mc), "r"(v.x), "r"(v.y),
+               "r"(v.z), "r"(v.w)
+               : "memory");
+}
+
+// Bounded wait until the counter at p reaches `target` (wrap-around compare);
+// on timeout records kStatusTimeoutAllReduce and returns false.
+__device__ __forceinline__ bool wait_counter_sys(const uint32_t* p, uint32_t target, uint64_t timeout_ns) {
+  uint64_t start = globaltimer();
+  for (;;) {
+    if ((int32_t)(ld_acquire_sys(p) - target) >= 0) return true;
+    if (globaltimer() - start > timeout_ns) {
+      atomicCAS(&g_status, 0, kStatusTimeoutAllReduce);
+      return false;
+    }
+    __nanosleep(128);
+  }
 }
 
 }  // namespace b2x

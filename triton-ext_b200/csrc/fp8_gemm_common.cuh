@@ -2,6 +2,7 @@
 #pragma once
 #include <cstdint>
 #include "b2x_ptx.cuh"
+#include "b2x_internal.h"
 
 namespace b2x {
 
@@ -29,6 +30,7 @@ struct GemmParams {
   int chunk3d;      // small-M kernel: A and B maps are 3-D (x, row, K chunk)
   int trace;        // record per-CTA wait cycles in g_trace
   int l2_a, l2_b;   // L2 policy per operand: 0 evict_last, 1 evict_normal, 2 evict_first
+  ArParams ar;      // fused all-reduce of C over the node's GPUs (paired kernel)
 };
 
 __device__ __forceinline__ uint64_t l2_policy(int which) {

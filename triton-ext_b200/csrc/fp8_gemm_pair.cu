@@ -29,6 +29,7 @@
 #include "b2x_ptx.cuh"
 #include "b2x_internal.h"
 #include "fp8_gemm_common.cuh"
+#include "fp8_gemm_allreduce.cuh"
 
 namespace b2x {
 
@@ -50,7 +51,10 @@ struct PairSmem {
   static constexpr int kAlloc = kBarOff + kBarBytes + 1024;
 };
 
-template <int STAGES, int B_MN>
+// AR: 0 plain GEMM; 1 / 2 the GEMM output is summed over the node's GPUs as
+// its units are stored (fp8_gemm_allreduce.cuh; 1 NVSwitch multicast, 2 peer
+// loads and stores).
+template <int STAGES, int B_MN, int AR>
 __global__ void __launch_bounds__(kThreads, 1)
     fp8_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                          const __grid_constant__ CUtensorMap tmC, const GemmParams p) {
@@ -66,6 +70,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* mma_done = tempty + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(mma_done + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  volatile uint32_t* ar_flag = tmem_slot + 2;  // one word per epilogue warpgroup (AR only)
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -252,8 +257,14 @@ __global__ void __launch_bounds__(kThreads, 1)
           bulk_commit_group();
         }
       }
+      if constexpr (AR != 0) ar_unit_stored<AR>(p, 2 * tile + (int)rank, m0, n0, wg_tid, bar_id, ar_flag + e);
     }
     if (wg_tid == 0) bulk_wait_group0();
+    if constexpr (AR != 0) {
+      // The output is complete here once every unit of this call has been
+      // reduced, by whichever rank finished it last.
+      if (e == 0 && wg_tid == 0 && !*abort_flag) wait_counter_sys(p.ar.sig_peer[p.ar.rank], p.ar.done_target, kArWaitNs);
+    }
   }
 
   tc_fence_before();
@@ -264,10 +275,10 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 }
 
-template <int STAGES, int B_MN>
+template <int STAGES, int B_MN, int AR>
 static cudaError_t launch_pair_t(const GemmLaunch& g, const GemmParams& p, cudaStream_t st) {
   using L = PairSmem<STAGES>;
-  auto kern = fp8_gemm_pair_kernel<STAGES, B_MN>;
+  auto kern = fp8_gemm_pair_kernel<STAGES, B_MN, AR>;
   cudaError_t e = ensure_smem_attr(reinterpret_cast<const void*>(kern), L::kAlloc);
   if (e != cudaSuccess) return e;
   cudaLaunchConfig_t cfg = {};
@@ -323,7 +334,10 @@ cudaError_t launch_fp8_gemm_pair(const GemmLaunch& g, cudaStream_t st) {
   p.ldc = g.ldc;
   p.l2_a = g.l2_a;
   p.l2_b = g.l2_b;
-  return g.b_mn ? launch_pair_t<S, 1>(g, p, st) : launch_pair_t<S, 0>(g, p, st);
+  p.ar = g.ar;
+  if (g.ar.mode == 1) return launch_pair_t<S, 0, 1>(g, p, st);  // fused all-reduce: K-major B only
+  if (g.ar.mode == 2) return launch_pair_t<S, 0, 2>(g, p, st);
+  return g.b_mn ? launch_pair_t<S, 1, 0>(g, p, st) : launch_pair_t<S, 0, 0>(g, p, st);
 }
 
 }  // namespace b2x
