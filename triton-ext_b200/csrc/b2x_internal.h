@@ -24,9 +24,10 @@ cudaError_t launch_amax(const void* x, b2x_dtype xt, int64_t rows, int64_t cols,
 
 // Fused all-reduce of the GEMM output over the GPUs of one node
 // (b2x_fp8_gemm_allreduce).  Signal buffer layout, in 32-bit words on every
-// rank: word 0 counts finished reductions (done), words
-// [kArArrive0, kArArrive0 + units) count, per 128 x 256 output unit, the ranks
-// whose partial has landed (kept on rank unit % world).
+// rank: word 0 counts finished reductions (done), word 1 the units this rank
+// reduced (diagnostic), words [kArArrive0, kArArrive0 + units) count, per
+// 128 x 256 output unit, the ranks whose partial has landed (kept on the
+// unit's owner rank, ar_owner in fp8_gemm_allreduce.cuh).
 constexpr int kArMaxRanks = 8;
 constexpr int kArArrive0 = 64;
 struct ArParams {

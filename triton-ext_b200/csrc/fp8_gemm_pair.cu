@@ -48,7 +48,8 @@ struct PairSmem {
   static constexpr int kCOff = kBOff + STAGES * kBBytes;
   static constexpr int kBarOff = kCOff + 2 * kCBytes;
   static constexpr int kBarBytes = (2 * STAGES + 5) * 8 + 16;
-  static constexpr int kAlloc = kBarOff + kBarBytes + 1024;
+  static constexpr int kQOff = (kBarOff + kBarBytes + 15) / 16 * 16;  // fused all-reduce queues
+  static constexpr int kAlloc = kQOff + 2 * (int)sizeof(ArQueue) + 1024;
 };
 
 // AR: 0 plain GEMM; 1 / 2 the GEMM output is summed over the node's GPUs as
@@ -70,7 +71,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* mma_done = tempty + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(mma_done + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
-  volatile uint32_t* ar_flag = tmem_slot + 2;  // one word per epilogue warpgroup (AR only)
+  volatile ArQueue* ar_queue = reinterpret_cast<volatile ArQueue*>(smem + L::kQOff);  // one per epilogue warpgroup
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -88,6 +89,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     mbar_init(mma_done, 1);
     *abort_flag = 0;
+    for (int i = 0; i < 2; ++i) ar_queue[i].head = ar_queue[i].count = 0;
     fence_barrier_init();
   }
   if (warp == 0 && lane == 0) {
@@ -257,12 +259,14 @@ __global__ void __launch_bounds__(kThreads, 1)
           bulk_commit_group();
         }
       }
-      if constexpr (AR != 0) ar_unit_stored<AR>(p, 2 * tile + (int)rank, m0, n0, wg_tid, bar_id, ar_flag + e);
+      if constexpr (AR != 0) ar_service<AR>(p, 2 * tile + (int)rank, wg_tid, bar_id, ar_queue + e);
     }
     if (wg_tid == 0) bulk_wait_group0();
     if constexpr (AR != 0) {
+      if (wg_all(*abort_flag == 0, bar_id))
+        ar_service<AR>(p, -1, wg_tid, bar_id, ar_queue + e);  // reduce the owned units still queued
       // The output is complete here once every unit of this call has been
-      // reduced, by whichever rank finished it last.
+      // reduced by its owner rank.
       if (e == 0 && wg_tid == 0 && !*abort_flag) wait_counter_sys(p.ar.sig_peer[p.ar.rank], p.ar.done_target, kArWaitNs);
     }
   }
