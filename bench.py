@@ -300,6 +300,8 @@ def main():
     ap.add_argument("--comm", default="fused", choices=["fused", "nccl"],
                     help="N>1: down GEMM with its all-reduce fused in-kernel, or followed by NCCL all-reduce")
     ap.add_argument("--fused-mode", default="auto", choices=["auto", "multicast", "peer"])
+    ap.add_argument("--down-sms", type=int, default=None,
+                    help="SMs for the fused down GEMM on its side stream (default: its FLOP share; 0 = serial)")
     args = ap.parse_args()
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -333,7 +335,8 @@ def main():
 
     peaks = load_peaks()
     from b2x.sharded import LlamaFP8LinearSet
-    ls = LlamaFP8LinearSet(rank, world, dev, comm=args.comm, fused_mode=args.fused_mode)
+    ls = LlamaFP8LinearSet(rank, world, dev, comm=args.comm, fused_mode=args.fused_mode,
+                           down_sms=args.down_sms)
     for _ in range(max(args.warmup, 3)):
         ls.step()
     torch.cuda.synchronize()
@@ -433,7 +436,8 @@ def main():
             "config": {"workload": "llama3-70b fp8 linear set @ 8192 tokens: qkv 8192x10240x8192, "
                                    "gate_up 8192x57344x8192, down 8192x8192x28672",
                        "parallelism": (f"qkv/gate_up N-sharded, down K-sharded + all-reduce (x{world}); "
-                                       + (f"all-reduce fused into the down GEMM ({ls.fused.mode})" if ls.fused
+                                       + (f"all-reduce fused into the down GEMM ({ls.fused.mode}; down on "
+                                          f"{ls.down_sms or 'all'} SMs, concurrent with qkv/gate_up)" if ls.fused
                                           else ("NCCL all-reduce overlapped on a side stream" if world > 1
                                                 else "single GPU"))),
                        "l2": "inputs larger than L2 (1.2 GB of fp8 operands per step)",

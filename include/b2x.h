@@ -254,13 +254,17 @@ B2X_API b2x_status b2x_read_device_status(int* status_out);
 /*
  * Wait-cycle trace of the last GEMM launches (diagnostics).  When the
  * environment variable B2X_TRACE=1 is set at the first GEMM call, every GEMM
- * kernel adds, per CTA, the clock cycles each role spent waiting into 8
- * counters: [0] producer waiting for a free stage, [1] MMA waiting for
- * loaded data, [2] MMA waiting for a free accumulator, [3]/[4] epilogue
- * warpgroup 0/1 waiting for an accumulator, [5] CTA lifetime, [6] MMA issue (from data ready to commit),
- * [7] tiles or K blocks processed.  Copies max_ctas x 8 counters to `out`
- * (blocking) and clears them.  Counterpart of the reference's clock64-based
- * timing (tlx.clock64, extensions/utlx/tlx/language/tlx/utility.py:108).
+ * kernel adds, per CTA, clock cycles and counts into 16 counters: [0]
+ * producer waiting for a free stage, [1] MMA waiting for loaded data, [2] MMA
+ * waiting for a free accumulator, [3]/[4] epilogue warpgroup 0/1 waiting for
+ * an accumulator, [5] CTA lifetime, [6] MMA issue (from data ready to
+ * commit), [7] tiles or K blocks processed; for b2x_fp8_gemm_allreduce also
+ * [8] reducing owned units, [9] waiting for peers' partials, [10]/[11] units
+ * reduced inside / after the tile loop, [12] the final wait for every rank's
+ * reductions, [13] tile-loop end to end of the remaining reductions.
+ * Copies max_ctas x 16 counters to `out` (blocking) and clears them.
+ * Counterpart of the reference's clock64-based timing (tlx.clock64,
+ * extensions/utlx/tlx/language/tlx/utility.py:108).
  */
 B2X_API b2x_status b2x_trace_read(uint64_t* out, int max_ctas, int* n_ctas);
 /* ABI version of the loaded library (B2X_ABI_VERSION). */

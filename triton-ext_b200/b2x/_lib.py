@@ -30,6 +30,7 @@ EXPORTED = (
 )
 
 AR_MAX_RANKS = 8
+TRACE_SLOTS = 16  # counters per CTA returned by b2x_trace_read
 
 
 class CastArgs(ctypes.Structure):
@@ -152,7 +153,7 @@ def launch_count() -> int:
 def read_trace(max_ctas: int = 148):
     """Per-CTA wait-cycle counters of the GEMM kernels (see b2x_trace_read)."""
     import numpy as np
-    buf = np.zeros((max_ctas, 8), np.uint64)
+    buf = np.zeros((max_ctas, TRACE_SLOTS), np.uint64)
     n = ctypes.c_int(0)
     check(lib().b2x_trace_read(buf.ctypes.data, max_ctas, ctypes.byref(n)))
     return buf[: n.value]

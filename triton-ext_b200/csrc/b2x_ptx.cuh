@@ -113,7 +113,11 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volati
 //   2 MMA waiting for a free accumulator    3 epilogue WG0 waiting for data
 //   4 epilogue WG1 waiting for data         5 CTA lifetime (thread 0)
 //   6 MMA issue (data ready to commit)      7 units processed by the CTA
-constexpr int kTraceSlots = 8;
+// and, for the fused GEMM + all-reduce (paired kernel):
+//   8 reducing owned units                  9 waiting for peers' arrivals (queue full / drain)
+//  10 units reduced inside the tile loop   11 units reduced after it (drain)
+//  12 final wait for every rank's reductions  13 tile-loop end to drain end
+constexpr int kTraceSlots = 16;
 constexpr int kTraceMaxCtas = 512;
 __device__ unsigned long long g_trace[kTraceMaxCtas * kTraceSlots];
 

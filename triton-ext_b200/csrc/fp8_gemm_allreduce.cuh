@@ -164,8 +164,11 @@ __device__ __forceinline__ void ar_service(const GemmParams& p, int unit, int wg
         const int u = q->unit[q->head];
         const uint32_t* ctr = ar.sig_peer[ar.rank] + kArArrive0 + u;
         bool ready = ld_acquire_sys(ctr) >= (uint32_t)ar.world;
-        if (!ready && (drain || q->count == kArQueue))
+        if (!ready && (drain || q->count == kArQueue)) {
+          const long long t0 = clock64();
           ready = wait_counter_sys(ctr, (uint32_t)ar.world, kArWaitNs);
+          trace_add(p.trace, 9, (unsigned long long)(clock64() - t0));
+        }
         if (ready) {
           st_relaxed_sys(const_cast<uint32_t*>(ctr), 0u);  // all arrived: reset for the next call
           q->head = (q->head + 1) % kArQueue;
@@ -182,9 +185,12 @@ __device__ __forceinline__ void ar_service(const GemmParams& p, int unit, int wg
     const int cmd = q->cmd;
     named_bar_sync(bar_id, 128);  // everyone has read cmd before thread 0 rewrites it
     if (cmd < 0) break;
+    const long long t0 = clock64();
     ar_reduce_unit<AR>(p, cmd, wg_tid);
     named_bar_sync(bar_id, 128);
     if (wg_tid == 0) {
+      trace_add(p.trace, 8, (unsigned long long)(clock64() - t0));
+      trace_add(p.trace, drain ? 11 : 10, 1);
       if constexpr (AR == 1) {
         multimem_red_add_release_sys(ar.sig_mc, 1u);
       } else {

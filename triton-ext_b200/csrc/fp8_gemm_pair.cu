@@ -105,6 +105,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   cluster_sync();  // barrier inits and TMEM allocation visible to the pair
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  const long long t_start = clock64();
   const int num_pid_in_group = p.group_size_m * p.num_pid_n;
   const int cluster_id = blockIdx.x >> 1;
   const int num_clusters = gridDim.x >> 1;
@@ -263,14 +264,21 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     if (wg_tid == 0) bulk_wait_group0();
     if constexpr (AR != 0) {
+      const long long t_drain = clock64();
       if (wg_all(*abort_flag == 0, bar_id))
         ar_service<AR>(p, -1, wg_tid, bar_id, ar_queue + e);  // reduce the owned units still queued
+      if (wg_tid == 0) trace_add(p.trace, 13, (unsigned long long)(clock64() - t_drain));
       // The output is complete here once every unit of this call has been
       // reduced by its owner rank.
-      if (e == 0 && wg_tid == 0 && !*abort_flag) wait_counter_sys(p.ar.sig_peer[p.ar.rank], p.ar.done_target, kArWaitNs);
+      if (e == 0 && wg_tid == 0 && !*abort_flag) {
+        const long long t0 = clock64();
+        wait_counter_sys(p.ar.sig_peer[p.ar.rank], p.ar.done_target, kArWaitNs);
+        trace_add(p.trace, 12, (unsigned long long)(clock64() - t0));
+      }
     }
   }
 
+  if (threadIdx.x == 0) trace_add(p.trace, 5, (unsigned long long)(clock64() - t_start));
   tc_fence_before();
   cluster_sync();  // no CTA leaves while its peer may still use its smem or barriers
   if (warp == 2) {
@@ -339,6 +347,7 @@ cudaError_t launch_fp8_gemm_pair(const GemmLaunch& g, cudaStream_t st) {
   p.l2_a = g.l2_a;
   p.l2_b = g.l2_b;
   p.ar = g.ar;
+  p.trace = g.trace;
   if (g.ar.mode == 1) return launch_pair_t<S, 0, 1>(g, p, st);  // fused all-reduce: K-major B only
   if (g.ar.mode == 2) return launch_pair_t<S, 0, 2>(g, p, st);
   return g.b_mn ? launch_pair_t<S, 1, 0>(g, p, st) : launch_pair_t<S, 0, 0>(g, p, st);
