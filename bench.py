@@ -288,13 +288,65 @@ def run_reference(args, rank, world):
     print(json.dumps(line), flush=True)
 
 
+def fused_down_report(args, rank, world, dev):
+    """N > 1: the down projection with its fused all-reduce alone (one kernel
+    per call), device-timed, max over ranks.  With B2X_TRACE=1 in the
+    environment also prints, per rank, the kernel's trace counters (include/b2x.h,
+    b2x_trace_read) averaged per call and over the CTAs that ran."""
+    import numpy as np
+    from b2x import _lib as L
+    from b2x.sharded import LlamaFP8LinearSet
+    if world < 2:
+        print(json.dumps({"workload": "fused-down", "skipped": "needs 2 or more ranks (torchrun)"}))
+        return
+    ls = LlamaFP8LinearSet(rank, world, dev, comm="fused", fused_mode=args.fused_mode, down_sms=0)
+    f = lambda: ls.fused(ls.a2, ls.sa2, ls.wd, ls.sd)  # noqa: E731
+    for _ in range(max(args.warmup, 3)):
+        f()
+    torch.cuda.synchronize()
+    dist.barrier()
+    tracing = os.environ.get("B2X_TRACE") == "1"
+    if tracing:
+        L.read_trace(512)
+    st, en = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    st.record()
+    for _ in range(args.steps):
+        f()
+    en.record()
+    torch.cuda.synchronize()
+    t = torch.tensor([st.elapsed_time(en) / args.steps], device=dev)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    row = {"rank": rank, "ms_per_call_max_over_ranks": round(t.item(), 4), "mode": ls.fused.mode}
+    if tracing:
+        tr = L.read_trace(512).astype(np.float64) / args.steps
+        tr = tr[tr[:, 5] > 0]  # CTAs that ran
+        mhz = float(torch.cuda.clock_rate(dev)) if hasattr(torch.cuda, "clock_rate") else 1965.0
+        us = lambda v: round(float(v) / mhz, 1)  # noqa: E731
+        row.update({
+            "ctas": int(tr.shape[0]), "sm_mhz_assumed": mhz,
+            "cta_life_us_mean": us(tr[:, 5].mean()), "cta_life_us_max": us(tr[:, 5].max()),
+            "reducing_us_per_cta": us(tr[:, 8].mean()), "waiting_for_peers_us_per_cta": us(tr[:, 9].mean()),
+            "units_reduced_in_loop": round(float(tr[:, 10].sum()), 1),
+            "units_reduced_after_loop": round(float(tr[:, 11].sum()), 1),
+            "us_per_reduced_unit": us(tr[:, 8].sum() / max(1.0, tr[:, 10].sum() + tr[:, 11].sum())),
+            "final_wait_us_mean": us(tr[:, 12].mean()), "final_wait_us_max": us(tr[:, 12].max()),
+        })
+    rows = [None] * world
+    dist.all_gather_object(rows, row)
+    if rank == 0:
+        for r in rows:
+            print(json.dumps(r), flush=True)
+    dist.barrier()
+    dist.destroy_process_group()
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=100)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="b2x", choices=["b2x", "reference"])
-    ap.add_argument("--workload", default="llama", choices=["llama", "gemm", "cast", "decode", "blockscaled"])
+    ap.add_argument("--workload", default="llama", choices=["llama", "gemm", "cast", "decode", "blockscaled", "fused-down"])
     ap.add_argument("--shape", default="8192,8192,8192")
     ap.add_argument("--no-side", action="store_true", help="skip the side measurements")
     ap.add_argument("--comm", default="fused", choices=["fused", "nccl"],
@@ -316,6 +368,9 @@ def main():
         dist.init_process_group("nccl", device_id=dev)
     import b2x
 
+    if args.workload == "fused-down":
+        fused_down_report(args, rank, world, dev)
+        return
     if args.workload != "llama":
         # profiling / side workloads: one kernel family, rank 0 style output
         M, N, K = (int(v) for v in args.shape.split(","))
