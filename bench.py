@@ -4,17 +4,20 @@ Headline (BASELINE.json metric): fp8 GEMM TFLOP/s on the Llama-3-70B-shaped
 fp8 linear set at 8192 tokens (QKV 8192x10240x8192, gate+up 8192x57344x8192,
 down 8192x8192x28672), e4m3 per-tensor scales, bf16 out.  At N GPUs the set
 is sharded: QKV and gate+up column-parallel (N-sharded, no collective), down
-row-parallel (K-sharded) followed by an NCCL all-reduce of the bf16 partial
-outputs.  `value` is the whole-job aggregate (total FLOPs / max-over-ranks
-time); total work is fixed as N grows ("strong" scaling).
+row-parallel (K-sharded) with the sum of its bf16 partial outputs over the
+GPUs fused into the down GEMM kernel (NVSwitch multicast; `--comm nccl` runs
+the GEMM followed by an NCCL all-reduce instead).  `value` is the whole-job
+aggregate (total FLOPs / max-over-ranks time); total work is fixed as N grows
+("strong" scaling).
 
 Side measurements on rank 0 (same JSON line): 8192^3 GEMM, the decode split-K
-GEMM, the block-scaled GEMM, the 64M-element cast (GB/s), cuBLASLt fp8
+GEMM, the block-scaled and MX GEMMs, the 64M-element cast (GB/s), cuBLASLt fp8
 (torch._scaled_mm) on 8192^3 for context, and the CPU oracle on a bounded
 sample of the headline workload (`cpu_baseline`).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b2x|reference]
-                    [--workload llama|gemm|cast|decode|blockscaled] [--shape M,N,K]
+                    [--workload llama|gemm|cast|decode|blockscaled|mx|fused-down] [--shape M,N,K]
+                    [--comm fused|nccl] [--fused-mode auto|multicast|peer] [--down-sms S]
 """
 import argparse
 import json
@@ -182,6 +185,9 @@ def gemm_tflops(M, N, K, iters=20, mode="tensor", cfg=None, dev="cuda"):
         A, sa = b2x.quantize(torch.randn((M, K), device=dev, generator=g), "block1x128", torch.float8_e4m3fn)
         W, sw = b2x.quantize(torch.randn((N, K), device=dev, generator=g), "block128x128", torch.float8_e4m3fn)
         sw = sw.t()
+    elif mode == "mx":
+        A, sa = b2x.quantize(torch.randn((M, K), device=dev, generator=g), "mx1x32", torch.float8_e4m3fn)
+        W, sw = b2x.quantize(torch.randn((N, K), device=dev, generator=g), "mx1x32", torch.float8_e4m3fn)
     else:
         A, sa = rand_fp8((M, K), g, dev)
         W, sw = rand_fp8((N, K), g, dev)
@@ -346,7 +352,7 @@ def main():
     ap.add_argument("--steps", type=int, default=100)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="b2x", choices=["b2x", "reference"])
-    ap.add_argument("--workload", default="llama", choices=["llama", "gemm", "cast", "decode", "blockscaled", "fused-down"])
+    ap.add_argument("--workload", default="llama", choices=["llama", "gemm", "cast", "decode", "blockscaled", "mx", "fused-down"])
     ap.add_argument("--shape", default="8192,8192,8192")
     ap.add_argument("--no-side", action="store_true", help="skip the side measurements")
     ap.add_argument("--comm", default="fused", choices=["fused", "nccl"],
@@ -380,6 +386,9 @@ def main():
         elif args.workload == "blockscaled":
             tf, ms = gemm_tflops(M, N, K, iters=args.steps, mode="block")
             print(json.dumps({"workload": "blockscaled", "shape": [M, N, K], "tflops": tf, "ms": ms}))
+        elif args.workload == "mx":
+            tf, ms = gemm_tflops(M, N, K, iters=args.steps, mode="mx")
+            print(json.dumps({"workload": "mx", "shape": [M, N, K], "tflops": tf, "ms": ms}))
         elif args.workload == "decode":
             tf, ms = gemm_tflops(64, 8192, 28672, iters=args.steps, cfg={"SPLIT_K": 8})
             print(json.dumps({"workload": "decode", "tflops": tf, "ms": ms,
@@ -475,6 +484,8 @@ def main():
         side["decode_frac_of_hbm"] = round(dbytes / (dms * 1e-3) / 1e9 / peaks["hbm_gbs"], 3)
         tf, _ = gemm_tflops(4096, 7168, 7168, mode="block")
         side["blockscaled_4096x7168x7168_tflops"] = round(tf, 1)
+        tf, _ = gemm_tflops(4096, 7168, 7168, mode="mx")
+        side["mx_e8m0_1x32_4096x7168x7168_tflops"] = round(tf, 1)
         side["cast_64M_gbs"] = cast_gbs(dev)
         side["cast_frac_of_hbm_f32_tensor"] = round(side["cast_64M_gbs"]["f32_tensor"] / peaks["hbm_gbs"], 3)
         try:

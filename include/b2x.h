@@ -148,6 +148,15 @@ typedef struct {
  *      scale_a + m*sa_stride_m + kb*sa_stride_k, scale_b[kb, nb] at
  *      scale_b + kb*sb_stride_k + nb*sb_stride_n; promotion per 128-deep
  *      K block: C = sum_kb sA[m,kb]*sB[kb,nb]*(A_kb.B_kb).
+ *   B2X_SCALE_MX_1x32: uint8 E8M0 scales, one per 32 K elements: scale_a
+ *      [M, K/32] with row stride sa_stride_m bytes, scale_b [N, K/32] (per
+ *      row of the [N, K] weight) with row stride sb_stride_n bytes:
+ *      C = sum_j 2^(sA[m,j]-127) * 2^(sB[n,j]-127) * (A_j . B_j), applied by
+ *      the tensor core (tcgen05 kind::mxf8f6f4.block_scale).  Needs K-major B,
+ *      K % 128 == 0, 4-byte aligned scale rows, and a workspace of
+ *      b2x_gemm_workspace_size bytes (any content; it receives the scales
+ *      re-tiled for the kernel).  Replaces async_dot_scaled with E8M0 scales
+ *      (extensions/utlx/python/utlx_plugin/mma_ops.py:163-237).
  * Split-K (config.split_k > 1): fp32 partials are reduced with
  * red.global.add.v4.f32 into a workspace; the last CTA to finish a tile
  * writes C.  The workspace must be all zero on the first call and is left all

@@ -214,7 +214,10 @@ def gemm(a_bits, b_bits_kn, a_fmt=E4M3, b_fmt=E4M3, scale_mode="tensor", scale_a
     """float64 C[M,N] for fp8 A[M,K] and B[K,N] (bytes) with the given scales.
 
     scale_mode "none" | "tensor" (scalars) | "block" (sA[M, KB], sB[KB, NB],
-    one scale per 128-deep K block; sB per 128x128 tile of the logical [K, N]).
+    one scale per 128-deep K block; sB per 128x128 tile of the logical [K, N])
+    | "mx" (uint8 E8M0 sA[M, K/32], sB[N, K/32]: each 32-deep K slice of a row
+    of A / column of B is multiplied by 2^(s - 127) -- the formula of the
+    reference's test_async_dot_scaled, test_tlx.py:2298-2444).
     """
     A = fp8_bits_to_f64(a_bits, a_fmt)
     B = fp8_bits_to_f64(b_bits_kn, b_fmt)
@@ -222,6 +225,13 @@ def gemm(a_bits, b_bits_kn, a_fmt=E4M3, b_fmt=E4M3, scale_mode="tensor", scale_a
         return A @ B
     if scale_mode == "tensor":
         return (A @ B) * float(np.float32(scale_a)) * float(np.float32(scale_b))
+    if scale_mode == "mx":
+        sa = np.asarray(scale_a, np.int64)
+        sb = np.asarray(scale_b, np.int64)
+        K = A.shape[1]
+        fa = np.ldexp(1.0, np.repeat(sa - 127, 32, axis=1)[:, :K])      # [M, K]
+        fb = np.ldexp(1.0, np.repeat(sb - 127, 32, axis=1)[:, :K]).T    # [K, N]
+        return (A * fa) @ (B * fb)
     if scale_mode == "block":
         M, K = A.shape
         N = B.shape[1]

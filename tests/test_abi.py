@@ -234,3 +234,29 @@ def test_default_config_keeps_caller_fields():
     assert (c.split_k, c.block_n) == (8, 128)
     c = _default_config(4096, 4096, 4096, kmajor=False)
     assert c.block_n >= 128  # row-major B is streamed in 128-column slabs
+
+
+def test_mx_gemm_rejects_bad_arguments():
+    L = _lib()
+    lib = L.lib()
+    ok = dict(scale_mode=L.SCALE_MX_1x32, scale_a=0x40000, scale_b=0x50000, sa_stride_m=8, sb_stride_n=8)
+    g = _gemm_args(**dict(ok, K=192, lda=256))  # K % 128 != 0
+    assert lib.b2x_fp8_gemm(ctypes.byref(g), None) == L.ERR_UNSUPPORTED
+    g = _gemm_args(**dict(ok, sa_stride_m=6))  # scale rows not 4-byte aligned / too short
+    assert lib.b2x_fp8_gemm(ctypes.byref(g), None) == L.ERR_INVALID_ARG
+    g = _gemm_args(**dict(ok, ldb_k=256, ldb_n=1))  # row-major B
+    assert lib.b2x_fp8_gemm(ctypes.byref(g), None) == L.ERR_UNSUPPORTED
+    g = _gemm_args(**ok)
+    assert lib.b2x_gemm_workspace_size(ctypes.byref(g)) > 0
+    assert lib.b2x_fp8_gemm(ctypes.byref(g), None) == L.ERR_WORKSPACE  # scale tiles need a workspace
+    g.config.block_n = 256  # MX tiles are 128 or 192 wide
+    assert lib.b2x_fp8_gemm(ctypes.byref(g), None) == L.ERR_UNSUPPORTED
+    assert b"MX" in lib.b2x_last_error()
+
+
+def test_mx_default_config_picks_an_mx_tile():
+    L = _lib()
+    g = _gemm_args(M=8192, N=8192, K=8192, lda=8192, ldc=8192, ldb_n=8192, scale_mode=L.SCALE_MX_1x32)
+    out = L.GemmConfig()
+    assert L.lib().b2x_gemm_default_config(ctypes.byref(g), ctypes.byref(out)) == L.OK
+    assert out.block_n in (128, 192) and out.num_ctas == 1 and out.split_k == 1

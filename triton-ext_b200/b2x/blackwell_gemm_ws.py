@@ -18,8 +18,11 @@ Differences a caller can see:
   for fp8 inputs b2x returns bfloat16 (or `out_dtype`), because an fp8
   output of an fp8 GEMM is not what fp8 inference wants.  fp16/bf16 inputs
   raise NotImplementedError: that GEMM is outside this library's path.
-* Optional keyword-only scale_a / scale_b: scalars (per-tensor, C = sA*sB*A.B)
-  or 2-D block scales (A: [M, ceil(K/128)], B: [ceil(K/128), ceil(N/128)]).
+* Optional keyword-only scale_a / scale_b: scalars (per-tensor, C = sA*sB*A.B),
+  2-D fp32 block scales (A: [M, ceil(K/128)], B: [ceil(K/128), ceil(N/128)]),
+  or 2-D uint8 E8M0 MX scales, one per 32 K elements (A: [M, K/32],
+  B: [N, K/32]), applied by the tensor core (the reference's async_dot_scaled,
+  extensions/utlx/python/utlx_plugin/mma_ops.py:163-237).
 * The CTA tile is 128 x BLOCK_SIZE_N x 128; config keys BLOCK_SIZE_M (128 or
   256), NUM_MMA_GROUPS, NUM_CTAS, NUM_SMEM_BUFFERS, NUM_TMEM_BUFFERS,
   EPILOGUE_SUBTILE, INTERLEAVE_EPILOGUE and USE_WARP_BARRIER are accepted and
@@ -268,7 +271,7 @@ def _to_b2x_config(cfg: dict, K: int) -> list:
     """Reference config dict -> b2x_gemm_config fields (see module docstring)."""
     bm = int(cfg.get("BLOCK_SIZE_M", 128))
     bn = int(cfg.get("BLOCK_SIZE_N", 0))
-    if bn and bn not in (64, 128, 256):
+    if bn and bn not in (64, 128, 192, 256):
         bn = min((64, 128, 256), key=lambda v: abs(v - bn))
     group = int(cfg.get("GROUP_SIZE_M", 0)) * max(1, bm // 128)
     sk = max(1, int(cfg.get("SPLIT_K", 1)))
@@ -288,6 +291,10 @@ def _scale_mode(scale_a, scale_b) -> str:
         return "none"
     if scale_a is None or scale_b is None:
         raise ValueError("pass both scale_a and scale_b, or neither")
+    if scale_a.dtype == torch.uint8 or scale_b.dtype == torch.uint8:
+        if scale_a.dtype != torch.uint8 or scale_b.dtype != torch.uint8 or scale_a.dim() != 2 or scale_b.dim() != 2:
+            raise ValueError("MX scales are two 2-D uint8 (E8M0) tensors: A [M, K/32] and B [N, K/32]")
+        return "mx"
     if scale_a.numel() == 1 and scale_b.numel() == 1:
         return "tensor"
     if scale_a.dim() == 2 and scale_b.dim() == 2:
@@ -305,7 +312,13 @@ def _autotune(a, b, scale_a, scale_b, mode, out_dtype):
         return _autotune_cache[key]
     base = ops.gemm_config(a, b, mode)
     cands = [[0] * 11]
-    if mode != "block":
+    if mode == "mx":
+        for bn in (192, 128):
+            c = [0] * 11
+            c[1] = bn
+            if c not in cands:
+                cands.append(c)
+    elif mode != "block":
         row_major_b = b.stride(1) == 1 and b.stride(0) != 1
         for bn in (256, 128, 64):
             if row_major_b and bn < 128:
@@ -379,6 +392,10 @@ def matmul(a, b, config=None, use_heuristic=False, *, scale_a: Optional[torch.Te
             if mode == "block":  # 128 or 256 (paired CTAs) wide tiles; libb2x picks when unset
                 cfg["BLOCK_SIZE_N"] = cfg.get("BLOCK_SIZE_N", 0) if cfg.get("BLOCK_SIZE_N", 0) in (128, 256) else 0
                 cfg["SPLIT_K"] = 1
+            elif mode == "mx":  # 128 or 192 wide single-CTA tiles
+                cfg["BLOCK_SIZE_N"] = cfg.get("BLOCK_SIZE_N", 0) if cfg.get("BLOCK_SIZE_N", 0) in (128, 192) else 0
+                cfg["SPLIT_K"] = 1
+                cfg["NUM_CTAS"] = 1
             fields = tuple(_to_b2x_config(cfg, K))
             if ckey is not None:
                 _config_cache[ckey] = fields

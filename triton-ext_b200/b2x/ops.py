@@ -25,7 +25,8 @@ CAST_MODES = {
     "block128x128": L.SCALE_BLOCK_128x128,
     "mx1x32": L.SCALE_MX_1x32,
 }
-GEMM_SCALE_MODES = {"none": L.SCALE_NONE, "tensor": L.SCALE_TENSOR, "block": L.SCALE_BLOCK_1x128}
+GEMM_SCALE_MODES = {"none": L.SCALE_NONE, "tensor": L.SCALE_TENSOR, "block": L.SCALE_BLOCK_1x128,
+                    "mx": L.SCALE_MX_1x32}
 CONFIG_FIELDS = ("block_m", "block_n", "block_k", "group_size_m", "num_smem_buffers", "num_tmem_buffers",
                  "num_mma_groups", "epilogue_subtile", "num_ctas", "split_k", "interleave_epilogue", "num_sms")
 
@@ -174,7 +175,9 @@ def _gemm_args(a, b, c, scale_mode, scale_a, scale_b, config: Sequence[int]) -> 
             g.sa_stride_m, g.sa_stride_k = scale_a.stride()
     if scale_b is not None:
         g.scale_b = scale_b.data_ptr()
-        if scale_b.dim() == 2:
+        if scale_mode == "mx":  # [N, K/32] bytes: row stride along N
+            g.sb_stride_n, g.sb_stride_k = scale_b.stride()
+        elif scale_b.dim() == 2:
             g.sb_stride_k, g.sb_stride_n = scale_b.stride()
     for name, v in zip(CONFIG_FIELDS, config):
         setattr(g.config, name, int(v))
@@ -229,7 +232,7 @@ def fp8_gemm_op(a: torch.Tensor, b: torch.Tensor, scale_a: Optional[torch.Tensor
     with torch.cuda.device(a.device):
         nws = lib.b2x_gemm_workspace_size(ctypes.byref(g))
         if nws:
-            ws = _workspace(a.device, nws, zeroed=True)
+            ws = _workspace(a.device, nws, zeroed=scale_mode != "mx")  # MX: scratch for tiled scales
             g.workspace, g.workspace_bytes = ws.data_ptr(), ws.numel()
         st = lib.b2x_fp8_gemm(ctypes.byref(g), ctypes.c_void_p(_stream(a.device)))
         if st != L.OK:
@@ -284,7 +287,7 @@ def fp8_gemm_fast(a: torch.Tensor, b: torch.Tensor, scale_a: Optional[torch.Tens
         with torch.cuda.device(dev):
             return fp8_gemm_fast(a, b, scale_a, scale_b, scale_mode, out_dtype, config)
     if nws:
-        ws = _workspace(dev, nws, zeroed=True)
+        ws = _workspace(dev, nws, zeroed=scale_mode != "mx")
         g.workspace, g.workspace_bytes = ws.data_ptr(), ws.numel()
     st = lib.b2x_fp8_gemm(ctypes.byref(g), ctypes.c_void_p(torch.cuda.current_stream(dev).cuda_stream))
     if st != L.OK:

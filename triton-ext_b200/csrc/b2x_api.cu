@@ -247,9 +247,27 @@ b2x_status b2x_gemm_default_config(const b2x_gemm_args* a, b2x_gemm_config* out)
     c.num_ctas = bs_pair ? 2 : 1;
     c.split_k = 1;
   }
+  if (a->scale_mode == B2X_SCALE_MX_1x32) {
+    // MX GEMM (fp8_gemm_mx.cu): 128 x 192 or 128 x 128 tiles on single CTAs
+    // (two accumulators and the scale factors must fit 512 TMEM columns).
+    if (c.block_n == 0) {
+      double best = -1;
+      const int bns[2] = {192, 128};
+      const double weight[2] = {1.0, 0.92};
+      for (int i = 0; i < 2; ++i) {
+        int64_t units = (int64_t)ceil_div(a->M, 128) * ceil_div(a->N, bns[i]);
+        int64_t waves = (units + sms - 1) / sms;
+        double eff = (double)units / (double)(waves * sms) * weight[i];
+        if (eff > best + 1e-9) best = eff, c.block_n = bns[i];
+      }
+    }
+    c.num_ctas = 1;
+    c.split_k = 1;
+  }
   // M <= 64 with a K-major B runs the operand-swapped small-M kernel: 128
   // weight rows per unit (fp8_gemm_smallm.cu).
-  const bool swap_ab = a->M <= 64 && !b_mn && !blockscaled && (c.block_n == 0 || c.block_n == 128);
+  const bool mx = a->scale_mode == B2X_SCALE_MX_1x32;
+  const bool swap_ab = a->M <= 64 && !b_mn && !blockscaled && !mx && (c.block_n == 0 || c.block_n == 128);
   if (swap_ab) c.block_n = 128;
   if (c.block_n == 0) {
     // Score each tile shape by how well its units fill the last wave, times
@@ -340,7 +358,7 @@ b2x_status b2x_gemm_default_config(const b2x_gemm_args* a, b2x_gemm_config* out)
   // Paired CTAs (256x256 tiles over two SMs) for large non-split problems:
   // a third less operand traffic per SM.  Needs 256-wide tiles and more
   // than one 128-row block of M.
-  const bool pair_ok = c.split_k == 1 && (c.block_n == 256 || blockscaled) && a->M > 128;
+  const bool pair_ok = c.split_k == 1 && (c.block_n == 256 || blockscaled) && a->M > 128 && !mx;
   if (c.num_ctas == 0) c.num_ctas = pair_ok ? 2 : 1;
   if (c.num_ctas == 2 && !pair_ok) c.num_ctas = 1;
   *out = c;
@@ -351,6 +369,8 @@ size_t b2x_gemm_workspace_size(const b2x_gemm_args* a) {
   if (!a) return 0;
   b2x_gemm_config c;
   if (b2x_gemm_default_config(a, &c) != B2X_OK) return 0;
+  if (a->scale_mode == B2X_SCALE_MX_1x32 && a->M > 0 && a->N > 0 && a->K > 0)
+    return mx_workspace_bytes(a->M, a->N, a->K, c.block_n);
   if (c.split_k <= 1) return 0;
   uint64_t tiles = (uint64_t)ceil_div(a->M, 128) * ceil_div(a->N, c.block_n);
   return (size_t)(align_up((uint64_t)a->M * a->N * 4, 256) + align_up(tiles * 4, 256));
@@ -402,14 +422,34 @@ static b2x_status fp8_gemm_impl(const b2x_gemm_args* a, const ArParams* ar, void
       if (!a->scale_a || !a->scale_b) return fail(B2X_ERR_INVALID_ARG, "b2x_fp8_gemm: NULL scale pointer");
       if (b_mn) return fail(B2X_ERR_UNSUPPORTED, "b2x_fp8_gemm: block-scaled GEMM needs a K-major B");
       break;
+    case B2X_SCALE_MX_1x32:
+      if (!a->scale_a || !a->scale_b) return fail(B2X_ERR_INVALID_ARG, "b2x_fp8_gemm: NULL scale pointer");
+      if (b_mn) return fail(B2X_ERR_UNSUPPORTED, "b2x_fp8_gemm: MX GEMM needs a K-major B");
+      if (a->K % 128)
+        return fail(B2X_ERR_UNSUPPORTED, "b2x_fp8_gemm: MX GEMM needs K %% 128 == 0 (got %lld)", (long long)a->K);
+      if (a->sa_stride_m < a->K / 32 || a->sb_stride_n < a->K / 32 || (a->sa_stride_m % 4) || (a->sb_stride_n % 4) ||
+          ((uintptr_t)a->scale_a % 4) || ((uintptr_t)a->scale_b % 4))
+        return fail(B2X_ERR_INVALID_ARG,
+                    "b2x_fp8_gemm: MX scales are uint8 [rows, K/32] with 4-byte aligned rows (sa_stride_m, "
+                    "sb_stride_n >= K/32 and %% 4 == 0)");
+      break;
     default:
       return fail(B2X_ERR_UNSUPPORTED, "b2x_fp8_gemm: scale mode %d not supported for GEMM", (int)a->scale_mode);
   }
+  const bool mx = a->scale_mode == B2X_SCALE_MX_1x32;
 
   b2x_gemm_config c;
   b2x_status s = b2x_gemm_default_config(a, &c);
   if (s != B2X_OK) return s;
-  if (c.block_n != 64 && c.block_n != 128 && c.block_n != 256)
+  if (mx) {
+    if (c.block_n != 128 && c.block_n != 192)
+      return fail(B2X_ERR_UNSUPPORTED, "b2x_fp8_gemm: MX GEMM runs 128- or 192-wide tiles (got %d)", c.block_n);
+    if (c.split_k > 1) return fail(B2X_ERR_UNSUPPORTED, "b2x_fp8_gemm: MX GEMM runs with SPLIT_K = 1");
+    const size_t need = mx_workspace_bytes(a->M, a->N, a->K, c.block_n);
+    if (!a->workspace || a->workspace_bytes < need || ((uintptr_t)a->workspace % 256))
+      return fail(B2X_ERR_WORKSPACE, "b2x_fp8_gemm: MX GEMM needs a %zu-byte workspace (256-byte aligned; got %zu)",
+                  need, a->workspace_bytes);
+  } else if (c.block_n != 64 && c.block_n != 128 && c.block_n != 256)
     return fail(B2X_ERR_UNSUPPORTED, "b2x_fp8_gemm: BLOCK_SIZE_N must be 64, 128 or 256 (got %d)", c.block_n);
   if (b_mn && c.block_n < 128)
     return fail(B2X_ERR_UNSUPPORTED, "b2x_fp8_gemm: row-major B needs BLOCK_SIZE_N >= 128");
@@ -467,8 +507,9 @@ static b2x_status fp8_gemm_impl(const b2x_gemm_args* a, const ArParams* ar, void
   // evict_first or evict_normal re-reads more under the power cap).
   g.l2_a = 0;
   g.l2_b = 0;
-  g.small_m = (!g.pair && !blockscaled && a->M <= 64) ? 1 : 0;
+  g.small_m = (!g.pair && !blockscaled && !mx && a->M <= 64) ? 1 : 0;
   g.swap_ab = (g.small_m && !b_mn && c.block_n == 128) ? 1 : 0;
+  if (mx) g.ws = reinterpret_cast<float*>(a->workspace);  // tiled scale atoms (fp8_gemm_mx.cu)
   if (c.split_k > 1) {
     g.ws = reinterpret_cast<float*>(a->workspace);
     g.counters = reinterpret_cast<int*>(reinterpret_cast<uint8_t*>(a->workspace) +
@@ -507,7 +548,9 @@ static b2x_status fp8_gemm_impl(const b2x_gemm_args* a, const ArParams* ar, void
       return fail(B2X_ERR_UNSUPPORTED, "b2x_fp8_gemm_allreduce: this shape does not run on the paired kernel");
     g.ar = *ar;
   }
-  if (blockscaled)
+  if (mx)
+    e = launch_fp8_gemm_mx(g, (cudaStream_t)stream);
+  else if (blockscaled)
     e = g.pair ? launch_fp8_gemm_blockscaled_pair(g, (cudaStream_t)stream)
                : launch_fp8_gemm_blockscaled(g, (cudaStream_t)stream);
   else if (g.pair)

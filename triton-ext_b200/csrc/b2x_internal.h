@@ -71,6 +71,8 @@ int smallm_tokens_tile(int64_t M);
 cudaError_t launch_fp8_gemm_pair(const GemmLaunch& g, cudaStream_t st);
 cudaError_t launch_fp8_gemm_blockscaled_pair(const GemmLaunch& g, cudaStream_t st);
 cudaError_t launch_fp8_gemm_blockscaled(const GemmLaunch& g, cudaStream_t st);
+cudaError_t launch_fp8_gemm_mx(const GemmLaunch& g, cudaStream_t st);
+size_t mx_workspace_bytes(int64_t M, int64_t N, int64_t K, int bn);
 cudaError_t launch_splitk_reduce(const void* ws, b2x_dtype wt, void* c, b2x_dtype ct, int64_t M, int64_t N,
                                  int64_t ldc, int split_k, cudaStream_t st);
 

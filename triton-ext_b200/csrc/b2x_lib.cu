@@ -7,5 +7,6 @@
 #include "fp8_gemm_smallm.cu"
 #include "fp8_gemm_blockscaled.cu"
 #include "fp8_gemm_blockscaled_pair.cu"
+#include "fp8_gemm_mx.cu"
 #include "splitk_reduce.cu"
 #include "fp8_gemm_noalloc.cu"
