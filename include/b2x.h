@@ -116,6 +116,22 @@ B2X_API b2x_status b2x_fp8_cast(const b2x_cast_args* args, void* stream);
 B2X_API b2x_status b2x_amax(const void* x, b2x_dtype x_type, int64_t rows, int64_t cols, int64_t ld_x, float* amax_out,
                     void* workspace, size_t workspace_bytes, void* stream);
 
+/*
+ * Stochastic rounding y = SR(x, r) of an fp32 [rows, cols] tensor to e4m3,
+ * e5m2, fp16 or bf16, with one uint32 of caller-given entropy per element
+ * (rbits [rows, cols], row stride ld_r).  |x| is truncated to the target's
+ * precision at its binade (subnormals included) and rounds up one quantum
+ * exactly when frac32 + r >= 2^32, where frac32 is the first 32 bits of the
+ * dropped remainder as a fraction of the quantum; so P(up) = frac32 / 2^32
+ * and E[y] = x up to 2^-32 of a quantum.  The sign is kept, values already
+ * representable are unchanged, results beyond the largest finite value
+ * (Inf included) saturate to +-max, NaN stays NaN.  Strides in elements.
+ * Replaces tlx.stoch_round(src, dst_ty, rand_bits),
+ * extensions/utlx/tlx/language/tlx/utility.py:113-153.
+ */
+B2X_API b2x_status b2x_stoch_round(const float* x, int64_t rows, int64_t cols, int64_t ld_x, const uint32_t* rbits,
+                                   int64_t ld_r, void* y, b2x_dtype y_type, int64_t ld_y, void* stream);
+
 /* ------------------------------------------------------------------ GEMM */
 
 /*

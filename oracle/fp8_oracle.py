@@ -305,3 +305,65 @@ def cast_input(n: int, seed: int = 0, sigma: float = 2.0, outlier_frac: float = 
         x[idx[:half]] = np.nan
         x[idx[half:]] = (np.inf * rng.choice([-1.0, 1.0], k - half)).astype(np.float32)
     return x
+
+
+# ----------------------------------------------------------------------------
+# Stochastic rounding (tlx.stoch_round, extensions/utlx/tlx/language/tlx/
+# utility.py:113-153; the rounding rule is stated in include/b2x.h,
+# b2x_stoch_round).  Integer restatement, one uint32 of entropy per element.
+
+SR_FORMATS = {"e4m3": (3, -6), "e5m2": (2, -14), "f16": (10, -14), "bf16": (7, -126)}
+
+
+def stoch_round_value(x: np.ndarray, r: np.ndarray, fmt: str) -> np.ndarray:
+    """float32 result of the stochastic truncation, before saturation/encoding."""
+    p, emin = SR_FORMATS[fmt]
+    x = np.asarray(x, np.float32)
+    bits = x.view(np.uint32).astype(np.int64)
+    r = np.asarray(r).astype(np.uint32).astype(np.int64)
+    sign = bits & 0x80000000
+    a = bits & 0x7FFFFFFF
+    E = a >> 23
+    F = a & 0x7FFFFF
+    sub = E == 0
+    M = np.where(sub, F, F | 0x800000)
+    e2 = np.where(sub, -149, E - 150)
+    with np.errstate(divide="ignore"):
+        lg = np.floor(np.log2(np.maximum(F, 1))).astype(np.int64)
+    eb = np.where(sub, -149 + lg, E - 127)
+    u = np.maximum(eb, emin) - p
+    s = u - e2
+    out = a.copy()  # s <= 0: representable already
+    need = (s > 0) & (a != 0) & (a < 0x7F800000)
+    ss = np.clip(s, 0, 63)
+    q = np.where(ss >= 56, 0, M >> np.minimum(ss, 55))
+    rem = np.where(ss >= 56, 0, M & ((np.int64(1) << np.minimum(ss, 55)) - 1))
+    frac32 = np.where(ss <= 32, (rem << np.clip(32 - ss, 0, 32)) & 0xFFFFFFFF, rem >> np.clip(ss - 32, 0, 63))
+    q = q + ((frac32 + r) >> 32)
+    val = q.astype(np.float64) * np.exp2(u.astype(np.float64))
+    with np.errstate(over="ignore"):
+        vbits = val.astype(np.float32).view(np.uint32).astype(np.int64)
+    out = np.where(need, vbits, out)
+    res = (out | sign).astype(np.uint32).view(np.float32)
+    return np.where(np.isnan(x), x, res)
+
+
+def stoch_round(x: np.ndarray, r: np.ndarray, fmt: str) -> np.ndarray:
+    """Encoded bits: uint8 for e4m3/e5m2, uint16 for f16/bf16 (saturating;
+    NaN -> the target's canonical NaN as the GPU's satfinite converts give it)."""
+    y = stoch_round_value(x, r, fmt)
+    if fmt in (E4M3, E5M2):
+        return f32_to_fp8_bits(y, fmt)
+    if fmt == "f16":
+        fmax = np.float32(65504.0)
+        with np.errstate(invalid="ignore"):
+            c = np.where(np.isnan(y), np.float32(np.nan), np.clip(y, -fmax, fmax)).astype(np.float32)
+        h = c.astype(np.float16).view(np.uint16)
+        return np.where(np.isnan(y), np.uint16(0x7FFF), h).astype(np.uint16)
+    # bf16: the value is exact in bf16 unless it overflowed; saturate to +-max
+    yb = y.view(np.uint32)
+    absb = yb & 0x7FFFFFFF
+    sat = (absb >= 0x7F800000) & ~np.isnan(y)
+    hi = (yb >> 16).astype(np.uint16)
+    hi = np.where(sat, ((yb >> 16) & 0x8000) | 0x7F7F, hi)
+    return np.where(np.isnan(y), np.uint16(0x7FFF), hi).astype(np.uint16)

@@ -145,3 +145,21 @@ def test_oracle_matches_golden(src, fmt, mode):
     if mode != "none":
         exp_s = g[f"s_{key}"].reshape(-1)
         assert np.array_equal(np.asarray(s).reshape(-1).view(np.uint8), exp_s.view(np.uint8))
+
+
+def test_stoch_round_oracle_rules():
+    """Representable values never move; r = 0 truncates toward zero; the
+    largest r rounds any inexact value up; saturation; unbiasedness."""
+    import fp8_oracle as O
+    x = np.array([1.0, 1.0625, -1.0625, 1.2, 500.0, -np.inf, 0.0], np.float32)
+    assert list(O.stoch_round(x, np.zeros(7, np.uint32), "e4m3")) == [0x38, 0x38, 0xB8, 0x39, 0x7E, 0xFE, 0x00]
+    assert list(O.stoch_round(x, np.full(7, 0xFFFFFFFF, np.uint32), "e4m3")) == [0x38, 0x39, 0xB9, 0x3A, 0x7E, 0xFE,
+                                                                                  0x00]
+    rng = np.random.default_rng(0)
+    n = 100000
+    v = np.full(n, 1.0001, np.float32)
+    r = rng.integers(0, 2 ** 32, n, dtype=np.uint64).astype(np.uint32)
+    h = O.stoch_round(v, r, "f16").view(np.float16).astype(np.float64)
+    assert abs(h.mean() - np.float64(np.float32(1.0001))) < 6 * 2 ** -10 / np.sqrt(n)
+    b = O.stoch_round(np.array([3.0e38, 5e-41], np.float32), np.array([0xFFFFFFFF, 0], np.uint32), "bf16")
+    assert b[0] == 0x7F62 and b[1] == 0x0000  # next bf16 up from 3.0e38; 5e-41 < 2^-133 truncates to 0 at r = 0

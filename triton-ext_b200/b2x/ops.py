@@ -333,3 +333,55 @@ def quantize(x: torch.Tensor, mode: str = "tensor", dtype: torch.dtype = torch.f
     """Quantize fp32/bf16 to fp8. Returns (q, scale) -- scale is None for mode 'none'."""
     q, sc = torch.ops.b2x.quantize(x, mode, dtype, scale)
     return q, (None if mode == "none" else sc)
+
+
+# ----------------------------------------------------------------------------
+# stochastic rounding
+
+SR_DTYPES = {torch.float8_e4m3fn: L.E4M3, torch.float8_e5m2: L.E5M2, torch.float16: L.F16,
+             torch.bfloat16: L.BF16}
+
+
+@torch.library.custom_op("b2x::stoch_round", mutates_args=())
+def stoch_round_op(src: torch.Tensor, dst_dtype: torch.dtype, rand_bits: torch.Tensor) -> torch.Tensor:
+    """fp32 -> e4m3 / e5m2 / fp16 / bf16 with one uint32 of entropy per
+    element; see include/b2x.h b2x_stoch_round."""
+    _require_cuda(src, rand_bits)
+    if src.dtype != torch.float32:
+        raise TypeError(f"stoch_round takes a float32 source, got {src.dtype}")
+    if dst_dtype not in SR_DTYPES:
+        raise TypeError(f"stoch_round targets float8_e4m3fn, float8_e5m2, float16 or bfloat16, got {dst_dtype}")
+    if rand_bits.shape != src.shape:
+        raise ValueError(f"rand_bits shape {tuple(rand_bits.shape)} must match src shape {tuple(src.shape)}")
+    if rand_bits.dtype not in (torch.int32, torch.uint32):
+        raise TypeError(f"rand_bits must be a 32-bit integer tensor, got {rand_bits.dtype}")
+    shape = src.shape
+    x = src.reshape(1, -1) if src.dim() <= 1 else src.reshape(-1, shape[-1])
+    r = rand_bits.reshape(1, -1) if rand_bits.dim() <= 1 else rand_bits.reshape(-1, shape[-1])
+    if x.stride(-1) != 1:
+        x = x.contiguous()
+    if r.stride(-1) != 1:
+        r = r.contiguous()
+    R, C = x.shape
+    y = torch.empty((R, C), dtype=dst_dtype, device=src.device)
+    if R * C:
+        with torch.cuda.device(src.device):
+            L.check(L.lib().b2x_stoch_round(x.data_ptr(), R, C, x.stride(0), r.data_ptr(), r.stride(0),
+                                            y.data_ptr(), SR_DTYPES[dst_dtype], C,
+                                            ctypes.c_void_p(_stream(src.device))))
+    return y.reshape(shape)
+
+
+@stoch_round_op.register_fake
+def _(src, dst_dtype, rand_bits):
+    return src.new_empty(src.shape, dtype=dst_dtype)
+
+
+def stoch_round(src: torch.Tensor, dst_ty: torch.dtype, rand_bits: torch.Tensor) -> torch.Tensor:
+    """Stochastic rounding of float32 `src` to `dst_ty` with one uint32 of
+    entropy per element (the reference's tlx.stoch_round(src, dst_ty,
+    rand_bits), extensions/utlx/tlx/language/tlx/utility.py:113-153).
+    Same-dtype requests return `src` unchanged, as the reference does."""
+    if dst_ty == src.dtype:
+        return src
+    return torch.ops.b2x.stoch_round(src, dst_ty, rand_bits)

@@ -623,6 +623,27 @@ b2x_status b2x_fp8_gemm_allreduce(const b2x_gemm_args* args, const b2x_allreduce
   return fp8_gemm_impl(&a, &ar, stream);
 }
 
+b2x_status b2x_stoch_round(const float* x, int64_t rows, int64_t cols, int64_t ld_x, const uint32_t* rbits,
+                           int64_t ld_r, void* y, b2x_dtype y_type, int64_t ld_y, void* stream) {
+  t_err[0] = 0;
+  if (y_type != B2X_E4M3 && y_type != B2X_E5M2 && y_type != B2X_F16 && y_type != B2X_BF16)
+    return fail(B2X_ERR_UNSUPPORTED, "b2x_stoch_round: target must be e4m3, e5m2, fp16 or bf16 (got %d)", (int)y_type);
+  if (rows < 0 || cols < 0) return fail(B2X_ERR_INVALID_ARG, "b2x_stoch_round: negative shape");
+  if (rows == 0 || cols == 0) return B2X_OK;
+  if (!x || !rbits || !y) return fail(B2X_ERR_INVALID_ARG, "b2x_stoch_round: NULL pointer");
+  if (ld_x < cols || ld_r < cols || ld_y < cols)
+    return fail(B2X_ERR_INVALID_ARG, "b2x_stoch_round: a row stride is smaller than cols");
+  const int out_bytes = (y_type == B2X_E4M3 || y_type == B2X_E5M2) ? 1 : 2;
+  if (((uintptr_t)x % 4) || ((uintptr_t)rbits % 4) || ((uintptr_t)y % out_bytes))
+    return fail(B2X_ERR_INVALID_ARG, "b2x_stoch_round: misaligned pointer");
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+  e = launch_stoch_round(x, rbits, y, y_type, rows, cols, ld_x, ld_r, ld_y, device_num_sms(dev), (cudaStream_t)stream);
+  if (e != cudaSuccess) return cuda_fail(e, "b2x_stoch_round launch");
+  return B2X_OK;
+}
+
 b2x_status b2x_trace_read(uint64_t* out, int max_ctas, int* n_ctas) {
   t_err[0] = 0;
   if (!out || max_ctas <= 0) return fail(B2X_ERR_INVALID_ARG, "b2x_trace_read: bad output buffer");

@@ -9,4 +9,5 @@
 #include "fp8_gemm_blockscaled_pair.cu"
 #include "fp8_gemm_mx.cu"
 #include "splitk_reduce.cu"
+#include "stoch_round.cu"
 #include "fp8_gemm_noalloc.cu"
