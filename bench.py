@@ -217,6 +217,21 @@ def cublas_fp8_tflops(M, N, K, iters=20, dev="cuda"):
         return f"unavailable: {type(e).__name__}"
 
 
+def stoch_round_gbs(dev="cuda", iters=20):
+    """64M-element stochastic rounding fp32 -> e4m3 / bf16 with one uint32 of
+    entropy per element; GB/s of algorithmic bytes (4 + 4 in, 1 or 2 out)."""
+    import b2x
+    n = 64 * 1024 * 1024
+    g = torch.Generator(device=dev).manual_seed(0)
+    x = torch.randn((8192, n // 8192), device=dev, generator=g)
+    r = torch.randint(-2 ** 31, 2 ** 31 - 1, x.shape, device=dev, dtype=torch.int32, generator=g)
+    out = {}
+    for name, dt, nb in (("e4m3", torch.float8_e4m3fn, 1), ("bf16", torch.bfloat16, 2)):
+        ms = graph_ms(lambda: b2x.stoch_round(x, dt, r), iters)  # noqa: B023
+        out[name] = round(n * (8 + nb) / (ms * 1e-3) / 1e9, 1)
+    return out
+
+
 def cast_gbs(dev="cuda", iters=20):
     """64M-element casts (BASELINE cast config), GB/s of algorithmic bytes."""
     import b2x
@@ -487,6 +502,7 @@ def main():
         tf, _ = gemm_tflops(4096, 7168, 7168, mode="mx")
         side["mx_e8m0_1x32_4096x7168x7168_tflops"] = round(tf, 1)
         side["cast_64M_gbs"] = cast_gbs(dev)
+        side["stoch_round_64M_gbs"] = stoch_round_gbs(dev)
         side["cast_frac_of_hbm_f32_tensor"] = round(side["cast_64M_gbs"]["f32_tensor"] / peaks["hbm_gbs"], 3)
         try:
             cpu = cpu_baseline_sample()
