@@ -231,6 +231,36 @@ B2X_API b2x_status b2x_splitk_reduce(const void* ws, b2x_dtype ws_type, void* c,
  */
 B2X_API b2x_status b2x_fp8_gemm_splitk_noalloc(const b2x_gemm_args* args, void* stream);
 
+/* ------------------------------------------------------------ grouped GEMM */
+
+/*
+ * Grouped fp8 GEMM: for every group g, C_g = sA_g * sB_g * (A_g . B_g^T) with
+ * A_g [M_g, K_g] (row stride lda), B_g the K-major [N_g, K_g] weight (row
+ * stride ldb) and C_g [M_g, N_g] bf16/fp16 (row stride ldc), all in one
+ * persistent launch.  Per-tensor scales are device pointers (both NULL: 1).
+ * Groups with M or N zero are skipped.  The workspace (64-byte aligned,
+ * b2x_grouped_gemm_workspace_size bytes) receives the group descriptors,
+ * copied from host memory on `stream` before the launch (so a call cannot be
+ * captured into a CUDA graph).  block_n: 0 picks 256 unless no group is wider
+ * than 128 columns.
+ * Replaces the reference's grouped GEMM, grouped_matmul_tlx_kernel with
+ * group_gemm_tlx_fn (extensions/utlx/tlx/tutorials/blackwell-grouped-gemm_test.py:366-784).
+ */
+typedef struct {
+  const void* a;
+  const void* b;
+  void* c;
+  int64_t M, N, K;
+  int64_t lda, ldb, ldc;
+  const float* scale_a;
+  const float* scale_b;
+} b2x_gemm_group;
+
+B2X_API size_t b2x_grouped_gemm_workspace_size(int num_groups);
+B2X_API b2x_status b2x_fp8_grouped_gemm(const b2x_gemm_group* groups, int num_groups, b2x_dtype a_type,
+                                        b2x_dtype b_type, b2x_dtype c_type, int block_n, void* workspace,
+                                        size_t workspace_bytes, void* stream);
+
 /* ------------------------------------------------------------ GEMM + all-reduce */
 
 /*

@@ -260,3 +260,26 @@ def test_mx_default_config_picks_an_mx_tile():
     out = L.GemmConfig()
     assert L.lib().b2x_gemm_default_config(ctypes.byref(g), ctypes.byref(out)) == L.OK
     assert out.block_n in (128, 192) and out.num_ctas == 1 and out.split_k == 1
+
+
+def test_grouped_gemm_rejects_bad_arguments():
+    L = _lib()
+    lib = L.lib()
+    assert lib.b2x_grouped_gemm_workspace_size(0) == 0
+    ws = lib.b2x_grouped_gemm_workspace_size(2)
+    assert ws >= 2 * 3 * 128
+    arr = (L.GemmGroup * 2)()
+    for g in arr:
+        g.a, g.b, g.c = 0x10000, 0x20000, 0x30000
+        g.M, g.N, g.K, g.lda, g.ldb, g.ldc = 128, 128, 128, 128, 128, 128
+    call = lambda groups, n, bn=0, w=0x40000, wb=ws: lib.b2x_fp8_grouped_gemm(groups, n, L.E4M3, L.E4M3, L.BF16,  # noqa: E731
+                                                                            bn, w, wb, None)
+    assert call(arr, 0) == L.OK
+    assert call(arr, 2, w=0) == L.ERR_WORKSPACE
+    assert call(arr, 2, bn=64) == L.ERR_UNSUPPORTED
+    arr[1].lda = 100
+    assert call(arr, 2) == L.ERR_INVALID_ARG
+    arr[1].lda = 128
+    arr[0].K = 0
+    assert call(arr, 2) == L.ERR_UNSUPPORTED
+    assert lib.b2x_fp8_grouped_gemm(arr, 2, L.BF16, L.E4M3, L.BF16, 0, 0x40000, ws, None) == L.ERR_UNSUPPORTED

@@ -27,7 +27,7 @@ EXPORTED = (
     "b2x_gemm_workspace_size", "b2x_fp8_gemm", "b2x_splitk_reduce", "b2x_last_error",
     "b2x_read_device_status", "b2x_abi_version", "b2x_launch_count", "b2x_fp8_gemm_splitk_noalloc",
     "b2x_trace_read", "b2x_allreduce_signal_words", "b2x_fp8_gemm_allreduce",
-    "b2x_stoch_round",
+    "b2x_stoch_round", "b2x_grouped_gemm_workspace_size", "b2x_fp8_grouped_gemm",
 )
 
 AR_MAX_RANKS = 8
@@ -70,6 +70,15 @@ class AllReduceArgs(ctypes.Structure):
         ("c_multicast", ctypes.c_void_p), ("c_peers", ctypes.c_void_p * AR_MAX_RANKS),
         ("signal_multicast", ctypes.c_void_p), ("signal_peers", ctypes.c_void_p * AR_MAX_RANKS),
         ("epoch", ctypes.c_uint32),
+    ]
+
+
+class GemmGroup(ctypes.Structure):
+    _fields_ = [
+        ("a", ctypes.c_void_p), ("b", ctypes.c_void_p), ("c", ctypes.c_void_p),
+        ("M", ctypes.c_int64), ("N", ctypes.c_int64), ("K", ctypes.c_int64),
+        ("lda", ctypes.c_int64), ("ldb", ctypes.c_int64), ("ldc", ctypes.c_int64),
+        ("scale_a", ctypes.c_void_p), ("scale_b", ctypes.c_void_p),
     ]
 
 
@@ -119,6 +128,12 @@ def lib() -> ctypes.CDLL:
         L.b2x_fp8_gemm.restype = ctypes.c_int
         L.b2x_trace_read.argtypes = [ctypes.c_void_p, ctypes.c_int, ctypes.POINTER(ctypes.c_int)]
         L.b2x_trace_read.restype = ctypes.c_int
+        L.b2x_grouped_gemm_workspace_size.argtypes = [ctypes.c_int]
+        L.b2x_grouped_gemm_workspace_size.restype = ctypes.c_size_t
+        L.b2x_fp8_grouped_gemm.argtypes = [ctypes.POINTER(GemmGroup), ctypes.c_int, ctypes.c_int, ctypes.c_int,
+                                           ctypes.c_int, ctypes.c_int, ctypes.c_void_p, ctypes.c_size_t,
+                                           ctypes.c_void_p]
+        L.b2x_fp8_grouped_gemm.restype = ctypes.c_int
         L.b2x_stoch_round.argtypes = [ctypes.c_void_p, ctypes.c_int64, ctypes.c_int64, ctypes.c_int64, ctypes.c_void_p,
                                        ctypes.c_int64, ctypes.c_void_p, ctypes.c_int, ctypes.c_int64, ctypes.c_void_p]
         L.b2x_stoch_round.restype = ctypes.c_int

@@ -385,3 +385,73 @@ def stoch_round(src: torch.Tensor, dst_ty: torch.dtype, rand_bits: torch.Tensor)
     if dst_ty == src.dtype:
         return src
     return torch.ops.b2x.stoch_round(src, dst_ty, rand_bits)
+
+
+# ----------------------------------------------------------------------------
+# grouped GEMM
+
+def grouped_gemm(group_A: Sequence[torch.Tensor], group_B: Sequence[torch.Tensor],
+                 scales_a: Optional[Sequence[torch.Tensor]] = None, scales_b: Optional[Sequence[torch.Tensor]] = None,
+                 out_dtype: torch.dtype = torch.bfloat16, block_n: int = 0) -> list:
+    """[A_g (M_g, K_g) fp8] x [B_g (N_g, K_g) fp8 weights] -> [C_g (M_g, N_g)] in one launch
+    (include/b2x.h b2x_fp8_grouped_gemm; the reference's group_gemm_tlx_fn,
+    blackwell-grouped-gemm_test.py:727-784, takes B as [N, K] the same way).
+    Optional per-tensor scales per group: C_g = sA_g * sB_g * A_g . B_g^T."""
+    if len(group_A) != len(group_B):
+        raise ValueError("group_A and group_B differ in length")
+    if (scales_a is None) != (scales_b is None):
+        raise ValueError("pass both scale lists or neither")
+    n = len(group_A)
+    if n == 0:
+        return []
+    _require_cuda(*group_A, *group_B)
+    dev = group_A[0].device
+    a_dt, b_dt = group_A[0].dtype, group_B[0].dtype
+    if a_dt not in FP8_DTYPES or b_dt not in FP8_DTYPES:
+        raise TypeError(f"grouped_gemm takes float8 operands, got {a_dt} x {b_dt}")
+    if out_dtype not in OUT_DTYPES:
+        raise TypeError(f"grouped_gemm output must be bfloat16 or float16, got {out_dtype}")
+    arr = (L.GemmGroup * n)()
+    outs, keep = [], []
+    for i, (A, B) in enumerate(zip(group_A, group_B)):
+        if A.dtype != a_dt or B.dtype != b_dt or A.device != dev or B.device != dev:
+            raise TypeError("all groups must share operand dtypes and device")
+        if A.dim() != 2 or B.dim() != 2 or A.shape[1] != B.shape[1]:
+            raise ValueError(f"group {i}: A {tuple(A.shape)} and B {tuple(B.shape)} are not [M, K] and [N, K]")
+        M, K = A.shape
+        N = B.shape[0]
+        if A.stride(1) != 1 or A.stride(0) % 16 or A.data_ptr() % 16:
+            A = _pad_k(A)
+        if B.stride(1) != 1 or B.stride(0) % 16 or B.data_ptr() % 16:
+            B = _pad_k(B)
+        n8 = -(-N // 8) * 8
+        C = torch.empty((M, n8), dtype=out_dtype, device=dev)[:, :N]
+        keep += [A, B]
+        outs.append(C)
+        g = arr[i]
+        g.a, g.b, g.c = A.data_ptr(), B.data_ptr(), C.data_ptr()
+        g.M, g.N, g.K = M, N, K
+        g.lda, g.ldb, g.ldc = A.stride(0), B.stride(0), C.stride(0)
+        if scales_a is not None:
+            sa = scales_a[i].to(torch.float32).reshape(1)
+            sb = scales_b[i].to(torch.float32).reshape(1)
+            keep += [sa, sb]
+            g.scale_a, g.scale_b = sa.data_ptr(), sb.data_ptr()
+    lib = L.lib()
+    with torch.cuda.device(dev):
+        nws = lib.b2x_grouped_gemm_workspace_size(n)
+        ws = _workspace(dev, nws + 64, zeroed=False)
+        base = ws.data_ptr()
+        off = (-base) % 64
+        L.check(lib.b2x_fp8_grouped_gemm(arr, n, FP8_DTYPES[a_dt], FP8_DTYPES[b_dt], OUT_DTYPES[out_dtype], block_n,
+                                         base + off, ws.numel() - off, ctypes.c_void_p(_stream(dev))))
+    return outs
+
+
+def _pad_k(t: torch.Tensor) -> torch.Tensor:
+    """Copy into a row-major buffer with a 16-element-aligned row pitch."""
+    R, K = t.shape
+    k16 = -(-K // 16) * 16
+    out = torch.zeros((R, k16), dtype=t.dtype, device=t.device)
+    out[:, :K] = t
+    return out[:, :K]

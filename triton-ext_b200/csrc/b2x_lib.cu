@@ -8,6 +8,7 @@
 #include "fp8_gemm_blockscaled.cu"
 #include "fp8_gemm_blockscaled_pair.cu"
 #include "fp8_gemm_mx.cu"
+#include "fp8_gemm_grouped.cu"
 #include "splitk_reduce.cu"
 #include "stoch_round.cu"
 #include "fp8_gemm_noalloc.cu"
