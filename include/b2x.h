@@ -231,6 +231,34 @@ B2X_API b2x_status b2x_splitk_reduce(const void* ws, b2x_dtype ws_type, void* c,
  */
 B2X_API b2x_status b2x_fp8_gemm_splitk_noalloc(const b2x_gemm_args* args, void* stream);
 
+/* ------------------------------------------------------------ gate+up GEMM with SwiGLU */
+
+/*
+ * The gate+up projection of a gated MLP fused with SwiGLU and the fp8
+ * quantization of its output:
+ *   [g | u] = A . B^T * scales   (B: the K-major [2I, K] weight whose rows are
+ *                                 gate rows 128j..128j+127 followed by up rows
+ *                                 128j..128j+127, j = 0 .. I/128 - 1)
+ *   h       = g / (1 + exp(-g)) * u                       (fp32, [M, I])
+ *   q       = fp8_rne_satfinite(clamp(h / s, -FMAX, FMAX)) written to h (row stride ld_h)
+ * with s either
+ *   B2X_SCALE_BLOCK_1x128:  one fp32 scale per (row, 128 columns of h),
+ *                           s = amax / FMAX, written to h_scale [M, I/128]
+ *                           (row stride ld_h_scale) -- the A operand scales of
+ *                           the block-scaled down projection;
+ *   B2X_SCALE_TENSOR_GIVEN: *h_scale supplied by the caller (delayed scaling);
+ *                           if h_amax is not NULL, max |h| is max-reduced into
+ *                           *h_amax (which the caller zeroes before the call).
+ * args is the gate+up GEMM as for b2x_fp8_gemm (per-tensor scales or none;
+ * args->c and c_type are ignored; N = 2I must be a multiple of 256).  The
+ * [M, 2I] product never leaves the chip.  No counterpart in the reference: it
+ * composes the GEMM epilogue (blackwell_gemm_ws.py:673-824) with the quantize
+ * recipe (mxfp8_utils.py:37-84).
+ */
+B2X_API b2x_status b2x_fp8_gemm_swiglu(const b2x_gemm_args* args, void* h, int64_t ld_h, b2x_dtype h_type,
+                                       b2x_scale_mode h_mode, float* h_scale, int64_t ld_h_scale, float* h_amax,
+                                       void* stream);
+
 /* ------------------------------------------------------------ grouped GEMM */
 
 /*

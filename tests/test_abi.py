@@ -283,3 +283,27 @@ def test_grouped_gemm_rejects_bad_arguments():
     arr[0].K = 0
     assert call(arr, 2) == L.ERR_UNSUPPORTED
     assert lib.b2x_fp8_grouped_gemm(arr, 2, L.BF16, L.E4M3, L.BF16, 0, 0x40000, ws, None) == L.ERR_UNSUPPORTED
+
+
+def test_swiglu_rejects_bad_arguments():
+    L = _lib()
+    lib = L.lib()
+    g = _gemm_args()
+    call = lambda g, h=0x60000, ld=128, ht=L.E4M3, m=L.SCALE_BLOCK_1x128, s=0x70000, lds=1: lib.b2x_fp8_gemm_swiglu(  # noqa: E731
+        ctypes.byref(g), h, ld, ht, m, s, lds, None, None)
+    assert call(g, ht=L.BF16) == L.ERR_UNSUPPORTED
+    assert call(g, m=L.SCALE_TENSOR) == L.ERR_UNSUPPORTED
+    assert call(_gemm_args(N=384, ldc=384)) == L.ERR_UNSUPPORTED  # 2I not a multiple of 256
+    assert call(g, ld=100) == L.ERR_INVALID_ARG
+    assert call(g, s=0) == L.ERR_INVALID_ARG
+    assert call(_gemm_args(ldb_k=256, ldb_n=1)) == L.ERR_UNSUPPORTED  # row-major B
+
+
+def test_interleave_gate_up_layout():
+    import torch
+    from b2x import ops
+    wg = torch.arange(256 * 2, dtype=torch.float32).reshape(256, 2)
+    wu = -wg
+    w = ops.interleave_gate_up(wg, wu)
+    assert torch.equal(w[:128], wg[:128]) and torch.equal(w[128:256], wu[:128])
+    assert torch.equal(w[256:384], wg[128:]) and torch.equal(w[384:], wu[128:])

@@ -455,3 +455,54 @@ def _pad_k(t: torch.Tensor) -> torch.Tensor:
     out = torch.zeros((R, k16), dtype=t.dtype, device=t.device)
     out[:, :K] = t
     return out[:, :K]
+
+
+# ----------------------------------------------------------------------------
+# gate+up GEMM fused with SwiGLU and fp8 quantization
+
+def interleave_gate_up(w_gate: torch.Tensor, w_up: torch.Tensor) -> torch.Tensor:
+    """[I, K] gate and up weights -> the [2I, K] weight gemm_swiglu expects:
+    gate rows 128j..128j+127, then up rows 128j..128j+127, for each j."""
+    if w_gate.shape != w_up.shape or w_gate.shape[0] % 128:
+        raise ValueError("gate and up weights must have the same [I, K] shape with I % 128 == 0")
+    I, K = w_gate.shape
+    return torch.stack([w_gate.reshape(I // 128, 128, K), w_up.reshape(I // 128, 128, K)], dim=1).reshape(2 * I, K)
+
+
+def gemm_swiglu(x: torch.Tensor, w_gu: torch.Tensor, scale_x: Optional[torch.Tensor] = None,
+                scale_w: Optional[torch.Tensor] = None, mode: str = "block1x128",
+                h_scale: Optional[torch.Tensor] = None, h_dtype: torch.dtype = torch.float8_e4m3fn,
+                h_amax: Optional[torch.Tensor] = None):
+    """h = fp8(silu(x . gate^T) * (x . up^T)) for the interleaved weight w_gu
+    [2I, K] (interleave_gate_up); see include/b2x.h b2x_fp8_gemm_swiglu.
+    mode "block1x128": returns (h [M, I], scales [M, I/128]);
+    mode "given": h_scale (one fp32) is used, returns (h, h_scale); if h_amax
+    (one fp32, zeroed by the caller) is given, max |h| is accumulated into it."""
+    _require_cuda(x, w_gu, scale_x, scale_w, h_scale, h_amax)
+    if x.dtype not in FP8_DTYPES or w_gu.dtype not in FP8_DTYPES or h_dtype not in FP8_DTYPES:
+        raise TypeError("gemm_swiglu takes float8 operands and produces float8 h")
+    if mode not in ("block1x128", "given"):
+        raise ValueError(f"mode must be 'block1x128' or 'given', got {mode!r}")
+    M, K = x.shape
+    N = w_gu.shape[0]
+    I = N // 2
+    b = w_gu.t()
+    x, b = _tma_friendly(x, b)
+    h = torch.empty((M, -(-I // 16) * 16), dtype=h_dtype, device=x.device)[:, :I]
+    if mode == "block1x128":
+        sc = torch.empty((M, I // 128 if I % 128 == 0 else I // 128 + 1), dtype=torch.float32, device=x.device)
+        ld_sc, smode = sc.stride(0), L.SCALE_BLOCK_1x128
+    else:
+        if h_scale is None:
+            raise ValueError("mode 'given' needs h_scale")
+        sc = h_scale.to(torch.float32).reshape(1)
+        ld_sc, smode = 1, L.SCALE_TENSOR_GIVEN
+    sm = "none" if scale_x is None else "tensor"
+    c = torch.empty((1, 8), dtype=torch.bfloat16, device=x.device)
+    g = _gemm_args(x, b, c, sm, scale_x, scale_w, (0,) * len(CONFIG_FIELDS))
+    g.c, g.ldc = None, N
+    with torch.cuda.device(x.device):
+        L.check(L.lib().b2x_fp8_gemm_swiglu(ctypes.byref(g), h.data_ptr(), h.stride(0), FP8_DTYPES[h_dtype], smode,
+                                            sc.data_ptr(), ld_sc, None if h_amax is None else h_amax.data_ptr(),
+                                            ctypes.c_void_p(_stream(x.device))))
+    return h, sc

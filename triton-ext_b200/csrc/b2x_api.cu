@@ -376,9 +376,22 @@ size_t b2x_gemm_workspace_size(const b2x_gemm_args* a) {
   return (size_t)(align_up((uint64_t)a->M * a->N * 4, 256) + align_up(tiles * 4, 256));
 }
 
-// The GEMM behind b2x_fp8_gemm and b2x_fp8_gemm_allreduce (ar != NULL: the
-// paired kernel with the fused all-reduce epilogue).
-static b2x_status fp8_gemm_impl(const b2x_gemm_args* a, const ArParams* ar, void* stream) {
+// Fused SwiGLU + fp8 quantize output of b2x_fp8_gemm_swiglu.
+struct SwArgs {
+  void* h;
+  int64_t ld_h;
+  int fmt, mode;  // fmt 0 e4m3 / 1 e5m2; mode 0 block 1x128 / 1 given per-tensor scale
+  float* scale;
+  int64_t ld_scale;
+  const float* given;
+  float* amax;
+};
+
+// The GEMM behind b2x_fp8_gemm, b2x_fp8_gemm_allreduce (ar != NULL: the
+// paired kernel with the fused all-reduce epilogue) and b2x_fp8_gemm_swiglu
+// (sw != NULL: the paired kernel with the SwiGLU + quantize epilogue).
+static b2x_status fp8_gemm_impl(const b2x_gemm_args* a, const ArParams* ar, void* stream,
+                                const SwArgs* sw = nullptr) {
   if (!a) return fail(B2X_ERR_INVALID_ARG, "b2x_fp8_gemm: args is NULL");
   if (!is_fp8(a->a_type) || !is_fp8(a->b_type))
     return fail(B2X_ERR_UNSUPPORTED, "b2x_fp8_gemm: A and B must be e4m3 or e5m2 (got %d, %d)", (int)a->a_type,
@@ -390,7 +403,7 @@ static b2x_status fp8_gemm_impl(const b2x_gemm_args* a, const ArParams* ar, void
   if (a->K == 0) return fail(B2X_ERR_UNSUPPORTED, "b2x_fp8_gemm: K == 0 (C would be all zero)");
   if (a->M >= (1LL << 31) || a->N >= (1LL << 31) || a->K >= (1LL << 31))
     return fail(B2X_ERR_UNSUPPORTED, "b2x_fp8_gemm: dimensions must be < 2^31");
-  if (!a->a || !a->b || !a->c) return fail(B2X_ERR_INVALID_ARG, "b2x_fp8_gemm: NULL A, B or C");
+  if (!a->a || !a->b || (!a->c && !sw)) return fail(B2X_ERR_INVALID_ARG, "b2x_fp8_gemm: NULL A, B or C");
   if (a->lda < a->K) return fail(B2X_ERR_INVALID_ARG, "b2x_fp8_gemm: lda (%lld) < K (%lld)", (long long)a->lda,
                                  (long long)a->K);
   if ((a->lda % 16) || ((uintptr_t)a->a % 16))
@@ -408,7 +421,7 @@ static b2x_status fp8_gemm_impl(const b2x_gemm_args* a, const ArParams* ar, void
     return fail(B2X_ERR_INVALID_ARG, "b2x_fp8_gemm: B strides (%lld, %lld) are not K-major or row-major",
                 (long long)a->ldb_k, (long long)a->ldb_n);
   }
-  if (a->ldc < a->N || (a->ldc % 8) || ((uintptr_t)a->c % 16))
+  if (!sw && (a->ldc < a->N || (a->ldc % 8) || ((uintptr_t)a->c % 16)))
     return fail(B2X_ERR_INVALID_ARG, "b2x_fp8_gemm: C must be 16-byte aligned with ldc >= N and ldc %% 8 == 0");
   const bool blockscaled = a->scale_mode == B2X_SCALE_BLOCK_1x128;
   switch (a->scale_mode) {
@@ -441,6 +454,11 @@ static b2x_status fp8_gemm_impl(const b2x_gemm_args* a, const ArParams* ar, void
   b2x_gemm_config c;
   b2x_status s = b2x_gemm_default_config(a, &c);
   if (s != B2X_OK) return s;
+  if (ar || sw) {  // fused epilogues run on the paired kernel's 256 x 256 tiles
+    c.num_ctas = 2;
+    c.block_n = 256;
+    c.split_k = 1;
+  }
   if (mx) {
     if (c.block_n != 128 && c.block_n != 192)
       return fail(B2X_ERR_UNSUPPORTED, "b2x_fp8_gemm: MX GEMM runs 128- or 192-wide tiles (got %d)", c.block_n);
@@ -528,6 +546,10 @@ static b2x_status fp8_gemm_impl(const b2x_gemm_args* a, const ArParams* ar, void
                   128, g.pair ? (uint32_t)c.block_n / 2 : (uint32_t)c.block_n, CU_TENSOR_MAP_SWIZZLE_128B,
                   "B (K-major)");
   if (s != B2X_OK) return s;
+  if (sw)  // the fp8 output h [M, N/2]: one 128 x 128-byte box per CTA tile
+    s = encode_2d(&g.tmC, CU_TENSOR_MAP_DATA_TYPE_UINT8, sw->h, (uint64_t)(a->N / 2), (uint64_t)a->M,
+                  (uint64_t)sw->ld_h, 128, 128, CU_TENSOR_MAP_SWIZZLE_128B, "h");
+  else
   s = encode_2d(&g.tmC, a->c_type == B2X_F16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16,
                 a->c, (uint64_t)a->N, (uint64_t)a->M, (uint64_t)a->ldc * 2, 64, 128, CU_TENSOR_MAP_SWIZZLE_128B, "C");
   if (s != B2X_OK) return s;
@@ -543,6 +565,17 @@ static b2x_status fp8_gemm_impl(const b2x_gemm_args* a, const ArParams* ar, void
     }
   }
 
+  if (sw) {
+    if (!g.pair || blockscaled || mx || b_mn)
+      return fail(B2X_ERR_UNSUPPORTED, "b2x_fp8_gemm_swiglu: this GEMM does not run on the paired kernel");
+    g.swiglu = 1;
+    g.sw_mode = sw->mode;
+    g.sw_fmt = sw->fmt;
+    g.sw_scale = sw->scale;
+    g.sw_ld_scale = sw->ld_scale;
+    g.sw_given = sw->given;
+    g.sw_amax = sw->amax;
+  }
   if (ar) {
     if (!g.pair || blockscaled || c.split_k != 1 || c.block_n != 256 || b_mn)
       return fail(B2X_ERR_UNSUPPORTED, "b2x_fp8_gemm_allreduce: this shape does not run on the paired kernel");
@@ -566,6 +599,48 @@ static b2x_status fp8_gemm_impl(const b2x_gemm_args* a, const ArParams* ar, void
 b2x_status b2x_fp8_gemm(const b2x_gemm_args* a, void* stream) {
   t_err[0] = 0;
   return fp8_gemm_impl(a, nullptr, stream);
+}
+
+b2x_status b2x_fp8_gemm_swiglu(const b2x_gemm_args* args, void* h, int64_t ld_h, b2x_dtype h_type,
+                               b2x_scale_mode h_mode, float* h_scale, int64_t ld_h_scale, float* h_amax,
+                               void* stream) {
+  t_err[0] = 0;
+  if (!args) return fail(B2X_ERR_INVALID_ARG, "b2x_fp8_gemm_swiglu: args is NULL");
+  if (h_type != B2X_E4M3 && h_type != B2X_E5M2)
+    return fail(B2X_ERR_UNSUPPORTED, "b2x_fp8_gemm_swiglu: h must be e4m3 or e5m2");
+  if (h_mode != B2X_SCALE_BLOCK_1x128 && h_mode != B2X_SCALE_TENSOR_GIVEN)
+    return fail(B2X_ERR_UNSUPPORTED, "b2x_fp8_gemm_swiglu: h scales are BLOCK_1x128 (computed) or TENSOR_GIVEN");
+  if (args->scale_mode != B2X_SCALE_NONE && args->scale_mode != B2X_SCALE_TENSOR &&
+      args->scale_mode != B2X_SCALE_TENSOR_GIVEN)
+    return fail(B2X_ERR_UNSUPPORTED, "b2x_fp8_gemm_swiglu: the gate+up GEMM takes per-tensor scales or none");
+  if (args->M <= 0 || args->N <= 0 || args->N % 256)
+    return fail(B2X_ERR_UNSUPPORTED, "b2x_fp8_gemm_swiglu: N (gate + up rows) must be a positive multiple of 256");
+  if (!(args->ldb_k == 1 && args->ldb_n >= args->K))
+    return fail(B2X_ERR_UNSUPPORTED, "b2x_fp8_gemm_swiglu: B must be K-major (interleaved [2I, K] weight)");
+  if (args->config.split_k > 1 || args->config.num_ctas == 1 ||
+      (args->config.block_n && args->config.block_n != 256))
+    return fail(B2X_ERR_UNSUPPORTED, "b2x_fp8_gemm_swiglu: runs on CTA pairs with 256-wide tiles and SPLIT_K = 1");
+  const int64_t I = args->N / 2;
+  if (!h || ld_h < I || (ld_h % 16) || ((uintptr_t)h % 16))
+    return fail(B2X_ERR_INVALID_ARG, "b2x_fp8_gemm_swiglu: h must be 16-byte aligned with ld_h >= N/2, %% 16 == 0");
+  if (!h_scale) return fail(B2X_ERR_INVALID_ARG, "b2x_fp8_gemm_swiglu: NULL h_scale");
+  if (h_mode == B2X_SCALE_BLOCK_1x128 && ld_h_scale < I / 128)
+    return fail(B2X_ERR_INVALID_ARG, "b2x_fp8_gemm_swiglu: ld_h_scale must be >= N/256");
+  SwArgs sw;
+  sw.h = h;
+  sw.ld_h = ld_h;
+  sw.fmt = h_type == B2X_E4M3 ? 0 : 1;
+  sw.mode = h_mode == B2X_SCALE_BLOCK_1x128 ? 0 : 1;
+  sw.scale = h_scale;
+  sw.ld_scale = ld_h_scale;
+  sw.given = h_scale;
+  sw.amax = h_amax;
+  b2x_gemm_args a = *args;
+  a.c_type = B2X_BF16;
+  a.config.block_n = 256;
+  a.config.num_ctas = 2;
+  a.config.split_k = 1;
+  return fp8_gemm_impl(&a, nullptr, stream, &sw);
 }
 
 size_t b2x_allreduce_signal_words(int64_t M, int64_t N) {

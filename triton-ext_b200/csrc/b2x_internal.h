@@ -63,6 +63,12 @@ struct GemmLaunch {
   int trace;         // B2X_TRACE=1: per-CTA wait cycles into g_trace
   int l2_a, l2_b;    // L2 eviction policy per operand (0 last, 1 normal, 2 first)
   ArParams ar;       // fused all-reduce (pair kernel only)
+  int swiglu;        // fused SwiGLU + fp8 quantize epilogue (pair kernel only)
+  int sw_mode, sw_fmt;
+  float* sw_scale;
+  int64_t sw_ld_scale;
+  const float* sw_given;
+  float* sw_amax;
 };
 
 cudaError_t launch_fp8_gemm(const GemmLaunch& g, cudaStream_t st);

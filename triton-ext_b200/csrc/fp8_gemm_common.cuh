@@ -31,6 +31,13 @@ struct GemmParams {
   int trace;        // record per-CTA wait cycles in g_trace
   int l2_a, l2_b;   // L2 policy per operand: 0 evict_last, 1 evict_normal, 2 evict_first
   ArParams ar;      // fused all-reduce of C over the node's GPUs (paired kernel)
+  // fused SwiGLU + fp8 quantize epilogue (paired kernel, fp8_gemm_swiglu.cuh)
+  int sw_mode;            // 0: 1x128 block scales written to sw_scale; 1: given scale, amax into sw_amax
+  int sw_fmt;             // 0: e4m3, 1: e5m2
+  float* sw_scale;        // [M, N/256] fp32 (mode 0)
+  int64_t sw_ld_scale;
+  const float* sw_given;  // mode 1
+  float* sw_amax;         // mode 1, optional: max |h| (atomicMax on the bits; start from 0)
 };
 
 __device__ __forceinline__ uint64_t l2_policy(int which) {

@@ -30,6 +30,7 @@
 #include "b2x_internal.h"
 #include "fp8_gemm_common.cuh"
 #include "fp8_gemm_allreduce.cuh"
+#include "fp8_gemm_swiglu.cuh"
 
 namespace b2x {
 
@@ -54,8 +55,9 @@ struct PairSmem {
 
 // AR: 0 plain GEMM; 1 / 2 the GEMM output is summed over the node's GPUs as
 // its units are stored (fp8_gemm_allreduce.cuh; 1 NVSwitch multicast, 2 peer
-// loads and stores).
-template <int STAGES, int B_MN, int AR>
+// loads and stores).  EPI: 1 = the fused SwiGLU + fp8 quantize epilogue
+// (fp8_gemm_swiglu.cuh; tmC then maps the fp8 output h).
+template <int STAGES, int B_MN, int AR, int EPI = 0>
 __global__ void __launch_bounds__(kThreads, 1)
     fp8_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                          const __grid_constant__ CUtensorMap tmC, const GemmParams p) {
@@ -222,42 +224,50 @@ __global__ void __launch_bounds__(kThreads, 1)
       const uint32_t t_row = tmem_base + e * kPairBN + ((uint32_t)(q * 32) << 16);
       const int m0 = pid_m * 2 * kBM + (int)rank * kBM;
       const int n0 = pid_n * kPairBN;
-#pragma unroll 1
-      for (int c0 = 0; c0 < kPairBN; c0 += 64) {
-        uint32_t v[64];
-        tmem_ld_32x32b_x32(t_row + c0, *reinterpret_cast<uint32_t(*)[32]>(&v[0]));
-        tmem_ld_32x32b_x32(t_row + c0 + 32, *reinterpret_cast<uint32_t(*)[32]>(&v[32]));
-        tmem_ld_wait();
-        if (c0 + 64 == kPairBN) {
-          // Whole accumulator read: hand the buffer back to the MMA warp before
-          // the last conversion and store.
+      if constexpr (EPI == 1) {
+        swiglu_quant_tile(p, &tmC, t_row, m0, pid_n, alpha, stage_c, bar_id, wg_tid, row, [&]() {
           tc_fence_before();
           named_bar_sync(bar_id, 128);
           if (wg_tid == 0) mbar_arrive_cluster_relaxed(tempty_leader);
-        }
-        uint32_t pk[32];
-#pragma unroll
-        for (int i = 0; i < 32; ++i) {
-          float lo = __fmul_rn(__uint_as_float(v[2 * i]), alpha);
-          float hi = __fmul_rn(__uint_as_float(v[2 * i + 1]), alpha);
-          if (p.c_half) {
-            __half2 h = __floats2half2_rn(lo, hi);
-            pk[i] = *reinterpret_cast<uint32_t*>(&h);
-          } else {
-            pk[i] = pack_bf16x2(lo, hi);
+        });
+      } else {
+#pragma unroll 1
+        for (int c0 = 0; c0 < kPairBN; c0 += 64) {
+          uint32_t v[64];
+          tmem_ld_32x32b_x32(t_row + c0, *reinterpret_cast<uint32_t(*)[32]>(&v[0]));
+          tmem_ld_32x32b_x32(t_row + c0 + 32, *reinterpret_cast<uint32_t(*)[32]>(&v[32]));
+          tmem_ld_wait();
+          if (c0 + 64 == kPairBN) {
+            // Whole accumulator read: hand the buffer back to the MMA warp before
+            // the last conversion and store.
+            tc_fence_before();
+            named_bar_sync(bar_id, 128);
+            if (wg_tid == 0) mbar_arrive_cluster_relaxed(tempty_leader);
           }
-        }
-        if (wg_tid == 0) bulk_wait_group_read0();
-        named_bar_sync(bar_id, 128);
-        const uint32_t srow = smem_u32(stage_c + row * 128);
+          uint32_t pk[32];
 #pragma unroll
-        for (int j = 0; j < 8; ++j)
-          st_shared_v4(srow + ((j ^ (row & 7)) << 4), pk[4 * j], pk[4 * j + 1], pk[4 * j + 2], pk[4 * j + 3]);
-        fence_proxy_async_smem();
-        named_bar_sync(bar_id, 128);
-        if (wg_tid == 0 && m0 < p.M) {  // the odd CTA's rows may lie wholly past M
-          tma_store_2d(&tmC, stage_c, n0 + c0, m0);
-          bulk_commit_group();
+          for (int i = 0; i < 32; ++i) {
+            float lo = __fmul_rn(__uint_as_float(v[2 * i]), alpha);
+            float hi = __fmul_rn(__uint_as_float(v[2 * i + 1]), alpha);
+            if (p.c_half) {
+              __half2 h = __floats2half2_rn(lo, hi);
+              pk[i] = *reinterpret_cast<uint32_t*>(&h);
+            } else {
+              pk[i] = pack_bf16x2(lo, hi);
+            }
+          }
+          if (wg_tid == 0) bulk_wait_group_read0();
+          named_bar_sync(bar_id, 128);
+          const uint32_t srow = smem_u32(stage_c + row * 128);
+#pragma unroll
+          for (int j = 0; j < 8; ++j)
+            st_shared_v4(srow + ((j ^ (row & 7)) << 4), pk[4 * j], pk[4 * j + 1], pk[4 * j + 2], pk[4 * j + 3]);
+          fence_proxy_async_smem();
+          named_bar_sync(bar_id, 128);
+          if (wg_tid == 0 && m0 < p.M) {  // the odd CTA's rows may lie wholly past M
+            tma_store_2d(&tmC, stage_c, n0 + c0, m0);
+            bulk_commit_group();
+          }
         }
       }
       if constexpr (AR != 0) ar_service<AR>(p, 2 * tile + (int)rank, wg_tid, bar_id, ar_queue + e);
@@ -287,10 +297,10 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 }
 
-template <int STAGES, int B_MN, int AR>
+template <int STAGES, int B_MN, int AR, int EPI = 0>
 static cudaError_t launch_pair_t(const GemmLaunch& g, const GemmParams& p, cudaStream_t st) {
   using L = PairSmem<STAGES>;
-  auto kern = fp8_gemm_pair_kernel<STAGES, B_MN, AR>;
+  auto kern = fp8_gemm_pair_kernel<STAGES, B_MN, AR, EPI>;
   cudaError_t e = ensure_smem_attr(reinterpret_cast<const void*>(kern), L::kAlloc);
   if (e != cudaSuccess) return e;
   cudaLaunchConfig_t cfg = {};
@@ -348,6 +358,13 @@ cudaError_t launch_fp8_gemm_pair(const GemmLaunch& g, cudaStream_t st) {
   p.l2_b = g.l2_b;
   p.ar = g.ar;
   p.trace = g.trace;
+  p.sw_mode = g.sw_mode;
+  p.sw_fmt = g.sw_fmt;
+  p.sw_scale = g.sw_scale;
+  p.sw_ld_scale = g.sw_ld_scale;
+  p.sw_given = g.sw_given;
+  p.sw_amax = g.sw_amax;
+  if (g.swiglu) return launch_pair_t<S, 0, 0, 1>(g, p, st);  // K-major B only
   if (g.ar.mode == 1) return launch_pair_t<S, 0, 1>(g, p, st);  // fused all-reduce: K-major B only
   if (g.ar.mode == 2) return launch_pair_t<S, 0, 2>(g, p, st);
   return g.b_mn ? launch_pair_t<S, 1, 0>(g, p, st) : launch_pair_t<S, 0, 0>(g, p, st);
