@@ -16,7 +16,8 @@ GEMM, the block-scaled and MX GEMMs, the 64M-element cast (GB/s), cuBLASLt fp8
 sample of the headline workload (`cpu_baseline`).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b2x|reference]
-                    [--workload llama|gemm|cast|decode|blockscaled|mx|fused-down] [--shape M,N,K]
+                    [--workload llama|gemm|cast|decode|blockscaled|mx|grouped|stochround|swiglu|fused-down]
+                    [--shape M,N,K]
                     [--comm fused|nccl] [--fused-mode auto|multicast|peer] [--down-sms S]
 """
 import argparse
@@ -217,6 +218,47 @@ def cublas_fp8_tflops(M, N, K, iters=20, dev="cuda"):
         return f"unavailable: {type(e).__name__}"
 
 
+MOE8 = [(m, 4096, 7168) for m in (2048, 1536, 2560, 2048, 1024, 3072, 2048, 2048)]
+
+
+def grouped_tflops(iters=10, shapes=MOE8, dev="cuda"):
+    """One grouped launch over 8 ragged MoE expert GEMMs (N 4096, K 7168)."""
+    import b2x
+    g = torch.Generator(device=dev).manual_seed(0)
+    A = [rand_fp8((M, K), g, dev) for (M, N, K) in shapes]
+    B = [rand_fp8((N, K), g, dev) for (M, N, K) in shapes]
+    f = lambda: b2x.grouped_gemm([a for a, _ in A], [b for b, _ in B], [s for _, s in A], [s for _, s in B])  # noqa: E731
+    for _ in range(3):
+        f()
+    ms = timed(f, iters)
+    fl = sum(2.0 * M * N * K for (M, N, K) in shapes)
+    return {"groups": len(shapes), "ms": round(ms, 4), "tflops": round(fl / (ms * 1e-3) / 1e12, 1)}
+
+
+def swiglu_ms(M, N2, K, iters=10, dev="cuda"):
+    """gate+up GEMM [M, K] x [N2, K]^T fused with SwiGLU and 1x128 fp8 quantize
+    of h [M, N2/2], against the same work unfused (GEMM to bf16, torch SwiGLU,
+    quantize)."""
+    import b2x
+    g = torch.Generator(device=dev).manual_seed(0)
+    x, sx = rand_fp8((M, K), g, dev)
+    w, sw = rand_fp8((N2, K), g, dev)
+    I = N2 // 2
+
+    def unfused():
+        c = b2x.matmul(x, w.t(), {}, scale_a=sx, scale_b=sw).view(M, I // 128, 2, 128)
+        h = torch.nn.functional.silu(c[:, :, 0].float()) * c[:, :, 1].float()
+        return b2x.quantize(h.reshape(M, I), "block1x128")
+
+    out = {}
+    for name, f in (("fused", lambda: b2x.gemm_swiglu(x, w, sx, sw)), ("unfused", unfused)):
+        for _ in range(3):
+            f()
+        out[name + "_ms"] = round(timed(f, iters), 4)
+    out["fused_gemm_tflops"] = round(2.0 * M * N2 * K / (out["fused_ms"] * 1e-3) / 1e12, 1)
+    return out
+
+
 def stoch_round_gbs(dev="cuda", iters=20):
     """64M-element stochastic rounding fp32 -> e4m3 / bf16 with one uint32 of
     entropy per element; GB/s of algorithmic bytes (4 + 4 in, 1 or 2 out)."""
@@ -367,7 +409,8 @@ def main():
     ap.add_argument("--steps", type=int, default=100)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="b2x", choices=["b2x", "reference"])
-    ap.add_argument("--workload", default="llama", choices=["llama", "gemm", "cast", "decode", "blockscaled", "mx", "fused-down"])
+    ap.add_argument("--workload", default="llama", choices=["llama", "gemm", "cast", "decode", "blockscaled", "mx", "grouped", "stochround", "swiglu",
+                             "fused-down"])
     ap.add_argument("--shape", default="8192,8192,8192")
     ap.add_argument("--no-side", action="store_true", help="skip the side measurements")
     ap.add_argument("--comm", default="fused", choices=["fused", "nccl"],
@@ -404,6 +447,12 @@ def main():
         elif args.workload == "mx":
             tf, ms = gemm_tflops(M, N, K, iters=args.steps, mode="mx")
             print(json.dumps({"workload": "mx", "shape": [M, N, K], "tflops": tf, "ms": ms}))
+        elif args.workload == "grouped":
+            print(json.dumps(dict(workload="grouped", **grouped_tflops(args.steps))))
+        elif args.workload == "stochround":
+            print(json.dumps({"workload": "stochround", "gbs": stoch_round_gbs(dev, iters=args.steps)}))
+        elif args.workload == "swiglu":
+            print(json.dumps(dict(workload="swiglu", shape=[M, N, K], **swiglu_ms(M, N, K, args.steps))))
         elif args.workload == "decode":
             tf, ms = gemm_tflops(64, 8192, 28672, iters=args.steps, cfg={"SPLIT_K": 8})
             print(json.dumps({"workload": "decode", "tflops": tf, "ms": ms,
@@ -501,6 +550,8 @@ def main():
         side["blockscaled_4096x7168x7168_tflops"] = round(tf, 1)
         tf, _ = gemm_tflops(4096, 7168, 7168, mode="mx")
         side["mx_e8m0_1x32_4096x7168x7168_tflops"] = round(tf, 1)
+        side["grouped_moe8_n4096_k7168"] = grouped_tflops()
+        side["swiglu_gate_up_8192x57344x8192"] = swiglu_ms(8192, 57344, 8192)
         side["cast_64M_gbs"] = cast_gbs(dev)
         side["stoch_round_64M_gbs"] = stoch_round_gbs(dev)
         side["cast_frac_of_hbm_f32_tensor"] = round(side["cast_64M_gbs"]["f32_tensor"] / peaks["hbm_gbs"], 3)

@@ -8,7 +8,7 @@
 // yields 128 x 128 values of h, and the epilogue writes h as fp8 directly:
 //
 //   g, u  = alpha * acc[:, 0:128], alpha * acc[:, 128:256]   (alpha = sA * sB)
-//   h     = g / (1 + exp(-g)) * u                            (fp32)
+//   h     = g / (1 + exp(-g)) * u      (fp32, fast exp and division)
 //   block 1x128 scales:  s = amax_row(|h|) / FMAX, inv = s == 0 ? 0 : 1 / s
 //   given scale s:       inv = 1 / s, and amax |h| is max-reduced into *amax
 //   q     = fp8_rne_satfinite(copysign(min(|h * inv|, FMAX), h * inv))
@@ -34,7 +34,7 @@ __device__ __forceinline__ float swiglu_clamp(float y, float m) {
 __device__ __forceinline__ float swiglu_h(uint32_t g_bits, uint32_t u_bits, float alpha) {
   const float g = __fmul_rn(__uint_as_float(g_bits), alpha);
   const float u = __fmul_rn(__uint_as_float(u_bits), alpha);
-  return __fmul_rn(__fdiv_rn(g, 1.0f + __expf(-g)), u);
+  return __fmul_rn(__fdividef(g, 1.0f + __expf(-g)), u);
 }
 
 // One epilogue warpgroup on one 128 x 256 accumulator (t_row: this thread's
