@@ -442,15 +442,17 @@ int cast_num_partials(int64_t nsegs, int num_sms) {
 template <typename T, int FP8>
 static cudaError_t launch_cast_t(const CastGeom& g, int mode, void* scale, int64_t ld_scale, uint32_t* partials,
                                  int num_sms, cudaStream_t st) {
-  constexpr int U = 4;  // 4 x 8 elements per lane per step (128 B of fp32 / 64 B of bf16 in flight)
+  // 8-element segments per lane per step: 4 for fp32 (128 B in flight per
+  // lane), 8 for bf16 (the same 128 B), so both keep as many bytes in flight.
+  constexpr int U = sizeof(T) == 4 ? 4 : 8;
   switch (mode) {
     case B2X_SCALE_NONE:
     case B2X_SCALE_TENSOR_GIVEN:
     case B2X_SCALE_TENSOR: {
       int np = 0;
       if (mode == B2X_SCALE_TENSOR) {
-        auto ak = amax_partial_kernel<T, 4>;
-        np = grid_for(g.nsegs, 4, std::min(8, resident_ctas(ak)), num_sms);
+        auto ak = amax_partial_kernel<T, U>;
+        np = grid_for(g.nsegs, U, std::min(8, resident_ctas(ak)), num_sms);
         ak<<<np, 256, 0, st>>>(g, partials);
         note_launch(1);
       }
@@ -463,7 +465,7 @@ static cudaError_t launch_cast_t(const CastGeom& g, int mode, void* scale, int64
     case B2X_SCALE_BLOCK_1x128: {
       // Row-block kernels do a shuffle reduction and two divisions per group:
       // a shallower unroll keeps more warps resident to hide that latency.
-      constexpr int UR = sizeof(T) == 4 ? 4 : 4;
+      constexpr int UR = 4;  // 8 for bf16 measured slower (2.1 vs 3.2 TB/s at 64M)
       auto k = quant_rowblock_kernel<T, FP8, 128, UR>;
       k<<<grid_for(g.nsegs, UR, resident_ctas(k), num_sms), 256, 0, st>>>(g, scale, ld_scale);
       note_launch(1);
