@@ -329,8 +329,8 @@ def run_reference(args, rank, world):
     import numpy as np
     K = 8192
     rng = np.random.default_rng(0)
-    a = rng.integers(0, 256, (64, K), dtype=np.uint8) & 0x77
-    b = rng.integers(0, 256, (512, K), dtype=np.uint8) & 0x77
+    a = rng.integers(0, 256, (256, K), dtype=np.uint8) & 0x77
+    b = rng.integers(0, 256, (2048, K), dtype=np.uint8) & 0x77
     for _ in range(args.warmup):
         OC.gemm_bf16(a, b, "e4m3", "e4m3", 1.0, 1.0)
     t0 = time.time()
@@ -344,9 +344,9 @@ def run_reference(args, rank, world):
         "warmup": args.warmup, "ms_per_step": dt * 1e3 / args.steps, "higher_is_better": True, "scaling": "strong",
         "vs_baseline": None, "dtype": "e4m3 in, fp32 acc, bf16 out", "data": "synthetic",
         "config": {"workload": "llama3-70b fp8 linear set @ 8192 tokens (bounded sample per step)",
-                   "sample": "64 rows x 512 cols x K=8192 of the gate+up GEMM per step"},
+                   "sample": "256 rows x 2048 cols x K=8192 of the gate+up GEMM per step"},
         "cpu_baseline": {"value": v, "unit": "TFLOP/s", "cores": OC.max_threads(), "kind": "port",
-                         "sample": "64x512x8192 block of the gate+up GEMM per step, C restatement of the "
+                         "sample": "256x2048x8192 block of the gate+up GEMM per step, C restatement of the "
                                    "reference GEMM (oracle/fp8_oracle.c)"},
         "e2e": {"value": v, "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
