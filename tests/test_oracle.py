@@ -163,3 +163,22 @@ def test_stoch_round_oracle_rules():
     assert abs(h.mean() - np.float64(np.float32(1.0001))) < 6 * 2 ** -10 / np.sqrt(n)
     b = O.stoch_round(np.array([3.0e38, 5e-41], np.float32), np.array([0xFFFFFFFF, 0], np.uint32), "bf16")
     assert b[0] == 0x7F62 and b[1] == 0x0000  # next bf16 up from 3.0e38; 5e-41 < 2^-133 truncates to 0 at r = 0
+
+
+def test_mx_gemm_oracle_matches_reference_formula():
+    """The MX GEMM oracle equals the formula of the reference's
+    test_async_dot_scaled (test_tlx.py:2298-2444): each operand's 32-wide K
+    slices multiplied by 2^(scale - 127), then one matmul (float64 here)."""
+    import torch
+    import fp8_oracle as O
+    rng = np.random.default_rng(5)
+    M, N, K = 16, 24, 128
+    qa, sa = O.quantize(rng.standard_normal((M, K), dtype=np.float32) * 30, "mx1x32", O.E4M3)
+    qb, sb = O.quantize(rng.standard_normal((N, K), dtype=np.float32) / 7, "mx1x32", O.E5M2)
+    a = torch.from_numpy(O.fp8_bits_to_f64(qa, O.E4M3))
+    b = torch.from_numpy(O.fp8_bits_to_f64(qb, O.E5M2))
+    fa = torch.pow(2.0, torch.from_numpy(sa.astype(np.float64) - 127)).repeat_interleave(32, dim=1)
+    fb = torch.pow(2.0, torch.from_numpy(sb.astype(np.float64) - 127)).repeat_interleave(32, dim=1)
+    want = ((a * fa) @ (b * fb).T).numpy()
+    got = O.gemm(qa, qb.T, O.E4M3, O.E5M2, "mx", sa, sb)
+    assert np.array_equal(got, want)
