@@ -537,7 +537,7 @@ def main():
 
     side = {}
     cpu = None
-    if rank == 0 and not args.no_side:
+    if rank == 0 and world == 1 and not args.no_side:  # side metrics and the CPU baseline: N = 1 only
         tf, gms = gemm_tflops(8192, 8192, 8192)
         side["gemm_8192_tflops"] = round(tf, 1)
         side["gemm_8192_frac_of_2x_bf16_burst"] = round(tf / (2 * peaks["bf16"]), 3)
