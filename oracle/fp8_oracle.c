@@ -13,6 +13,9 @@
  * gemm: C = sA * sB * (A . B) with fp32 accumulation and a bf16 result, the
  *   arithmetic of matmul_kernel_tma_ws_blackwell (blackwell_gemm_ws.py:1089)
  *   on fp8 operands; B is taken K-major ([N][K]).
+ * stoch_round: tlx.stoch_round (extensions/utlx/tlx/language/tlx/utility.py:
+ *   113-153) with one uint32 of entropy per element, restated in floating
+ *   point (the numpy oracle restates it with integers; tests compare the two).
  */
 #include <math.h>
 #include <stdint.h>
@@ -282,4 +285,59 @@ double oracle_gemm_bf16(const uint8_t* A, int64_t lda, int a_fmt, const uint8_t*
   parallel_for((n1 - n0 + GEMM_NB - 1) / GEMM_NB, gemm_colblock, g);
   free(g);
   return 2.0 * (double)(m1 - m0) * (double)(n1 - n0) * (double)K;
+}
+
+/* ------------------------------------------------------------------------
+ * Stochastic rounding (tlx.stoch_round, extensions/utlx/tlx/language/tlx/
+ * utility.py:113-153), restated with floating-point arithmetic instead of the
+ * integer formulation of fp8_oracle.py:  t = |x| / q exactly (q the target's
+ * quantum at |x|), frac32 = floor((t - floor(t)) * 2^32), round up iff
+ * frac32 + r >= 2^32, then a saturating encode.  fmt: 0 e4m3, 1 e5m2,
+ * 2 fp16, 3 bf16.  Output: uint8 (fp8) or uint16 (fp16 / bf16) codes.
+ */
+static uint16_t encode_half(double v, int fp16) {
+  /* v is exactly representable in the target or beyond its range (saturate). */
+  const int mb = fp16 ? 10 : 7, bias = fp16 ? 15 : 127, emin = fp16 ? -14 : -126;
+  const double vmax = fp16 ? 65504.0 : ldexp(2.0 - ldexp(1.0, -7), 127);
+  uint16_t sign = signbit(v) ? 0x8000 : 0;
+  double a = fabs(v);
+  if (a >= vmax) return (uint16_t)(sign | (fp16 ? 0x7BFF : 0x7F7F));
+  if (a == 0.0) return sign;
+  int e;
+  frexp(a, &e); /* a = f * 2^e, f in [0.5, 1) */
+  e -= 1;       /* a in [2^e, 2^(e+1)) */
+  if (e < emin) return (uint16_t)(sign | (uint16_t)llround(a / ldexp(1.0, emin - mb)));
+  uint32_t m = (uint32_t)llround(a / ldexp(1.0, e - mb)) - (1u << mb);
+  return (uint16_t)(sign | ((uint32_t)(e + bias) << mb) | m);
+}
+
+void oracle_stoch_round(const float* x, const uint32_t* r, int64_t n, int fmt, void* out) {
+  static const int P[4] = {3, 2, 10, 7}, EMIN[4] = {-6, -14, -14, -126};
+  for (int64_t i = 0; i < n; ++i) {
+    const float xi = x[i];
+    double y;
+    if (isnan(xi)) {
+      y = NAN;
+    } else if (isinf(xi)) {
+      y = xi;
+    } else if (xi == 0.0f) {
+      y = xi;
+    } else {
+      const double a = fabs((double)xi);
+      int e;
+      frexp(a, &e);
+      e -= 1;
+      const int ue = (e > EMIN[fmt] ? e : EMIN[fmt]) - P[fmt];
+      const double t = ldexp(a, -ue); /* exact */
+      const double q = floor(t);
+      const double f32 = floor((t - q) * 4294967296.0);
+      const double up = (f32 + (double)r[i] >= 4294967296.0) ? 1.0 : 0.0;
+      y = copysign(ldexp(q + up, ue), (double)xi);
+    }
+    if (fmt <= 1) {
+      ((uint8_t*)out)[i] = isnan(y) ? (uint8_t)(0x7F | (signbit(xi) ? 0x80 : 0)) : to_fp8((float)y, fmt);
+    } else {
+      ((uint16_t*)out)[i] = isnan(y) ? (uint16_t)0x7FFF : encode_half(y, fmt == 2);
+    }
+  }
 }

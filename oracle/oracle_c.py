@@ -32,6 +32,9 @@ def lib():
                                        ctypes.c_int]
         L.oracle_gemm_bf16.restype = ctypes.c_double
         L.oracle_max_threads.restype = ctypes.c_int
+        L.oracle_stoch_round.argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int64, ctypes.c_int,
+                                         ctypes.c_void_p]
+        L.oracle_stoch_round.restype = None
         _lib = L
     return _lib
 
@@ -71,3 +74,15 @@ def gemm_bf16(a_bits, bt_bits, a_fmt, b_fmt, sa, sb, rows=None, cols=None, nthre
 
 def max_threads():
     return lib().oracle_max_threads()
+
+
+SR_FMTS = {"e4m3": 0, "e5m2": 1, "f16": 2, "bf16": 3}
+
+
+def stoch_round(x, r, fmt):
+    """Codes of the stochastic rounding of float32 x with uint32 entropy r."""
+    x = np.ascontiguousarray(x, np.float32).reshape(-1)
+    r = np.ascontiguousarray(r, np.uint32).reshape(-1)
+    out = np.empty(x.size, np.uint8 if fmt in ("e4m3", "e5m2") else np.uint16)
+    lib().oracle_stoch_round(x.ctypes.data, r.ctypes.data, x.size, SR_FMTS[fmt], out.ctypes.data)
+    return out

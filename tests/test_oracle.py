@@ -182,3 +182,22 @@ def test_mx_gemm_oracle_matches_reference_formula():
     want = ((a * fa) @ (b * fb).T).numpy()
     got = O.gemm(qa, qb.T, O.E4M3, O.E5M2, "mx", sa, sb)
     assert np.array_equal(got, want)
+
+
+@pytest.mark.parametrize("fmt", ["e4m3", "e5m2", "f16", "bf16"])
+def test_stoch_round_c_and_numpy_oracles_agree(fmt):
+    """Two restatements of the stochastic-rounding rule -- integer (numpy) and
+    floating-point (C) -- agree bit for bit, specials included."""
+    import fp8_oracle as O
+    import oracle_c as OC
+    rng = np.random.default_rng(11)
+    n = 200000
+    x = rng.standard_normal(n).astype(np.float32) * np.exp2(rng.integers(-140, 120, n)).astype(np.float32)
+    x[:16] = [0.0, -0.0, np.inf, -np.inf, np.nan, 448.0, 464.0, 57344.0, 65504.0, 65520.0, 3.0e38, 1e-45,
+              -1e-40, 2.0 ** -126, 1.0625, -1.0625]
+    r = rng.integers(0, 2 ** 32, n, dtype=np.uint64).astype(np.uint32)
+    r[:4] = [0, 0xFFFFFFFF, 0x80000000, 1]
+    a = O.stoch_round(x, r, fmt)
+    b = OC.stoch_round(x, r, fmt)
+    bad = np.nonzero(a != b)[0]
+    assert bad.size == 0, (fmt, bad[:5], x[bad[:5]], r[bad[:5]], a[bad[:5]], b[bad[:5]])
