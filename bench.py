@@ -1,6 +1,6 @@
 """Benchmark: B200-native fp8 GEMM / fp8 cast / split-K (b2x).
 
-Headline (BASELINE.json metric): fp8 GEMM TFLOP/s on the Llama-3-70B-shaped
+Headline metric: fp8 GEMM TFLOP/s on the Llama-3-70B-shaped
 fp8 linear set at 8192 tokens (QKV 8192x10240x8192, gate+up 8192x57344x8192,
 down 8192x8192x28672), e4m3 per-tensor scales, bf16 out.  At N GPUs the set
 is sharded: QKV and gate+up column-parallel (N-sharded, no collective), down
@@ -275,7 +275,7 @@ def stoch_round_gbs(dev="cuda", iters=20):
 
 
 def cast_gbs(dev="cuda", iters=20):
-    """64M-element casts (BASELINE cast config), GB/s of algorithmic bytes."""
+    """64M-element casts (the cast benchmark configuration), GB/s of algorithmic bytes."""
     import b2x
     import fp8_oracle as O
     n = 64 * 1024 * 1024

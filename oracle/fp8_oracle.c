@@ -1,5 +1,5 @@
 /*
- * C restatement of the b2x fp8 path -- TEST INFRASTRUCTURE / CPU BASELINE ONLY.
+ * C restatement of the b2x fp8 path -- TEST INFRASTRUCTURE / TIMED CPU REFERENCE ONLY.
  *
  * Used by tests/ (cross-checked against oracle/fp8_oracle.py) and by bench.py
  * as the timed CPU baseline and the `--impl reference` arm.  Never linked

@@ -24,7 +24,7 @@ recipe and its scaled fp8 GEMM:
   becomes +FMAX.  Divisions are IEEE fp32
   divisions and the multiply is a single rounded fp32 multiply.  The same
   recipe with one scale per tensor, per 1x128 row block or per 128x128 tile
-  gives the other scale modes (no reference test pins them).
+  gives the other scale modes (the benchmark configurations; no reference test pins them).
 
 * GEMM -- matmul of blackwell_gemm_ws.py:1352 on fp8 inputs with the scaled
   reference formula of test_async_dot_scaled (extensions/utlx/test/
@@ -285,7 +285,7 @@ def bf16_round(x: np.ndarray) -> np.ndarray:
 
 
 # ----------------------------------------------------------------------------
-# Seeded synthetic inputs with the BASELINE configs' distributions.
+# Seeded synthetic inputs with the benchmark configurations' distributions.
 
 
 def cast_input(n: int, seed: int = 0, sigma: float = 2.0, outlier_frac: float = 0.01,

@@ -1,5 +1,5 @@
 """ctypes loader for liboracle.so (the C restatement in fp8_oracle.c).
-TEST INFRASTRUCTURE / CPU BASELINE ONLY -- see fp8_oracle.py."""
+TEST INFRASTRUCTURE / TIMED CPU REFERENCE ONLY -- see fp8_oracle.py."""
 import ctypes
 import os
 import subprocess

@@ -166,7 +166,7 @@ def test_fused_allreduce_modes_and_repeats():
 
 
 def test_fused_allreduce_bench_shape_rows():
-    """The BASELINE down projection (8192 x 8192, K = 28672 split over the
+    """The benchmark's down projection (8192 x 8192, K = 28672 split over the
     ranks), on a 1024-row slice so the float64 oracle stays quick."""
     import fp8_oracle as O
     world = _world()

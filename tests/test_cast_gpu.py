@@ -101,7 +101,7 @@ def test_amax_nan_ignoring():
 @pytest.mark.parametrize("src", ["f32", "bf16"])
 @pytest.mark.parametrize("mode", ["tensor", "block1x128"])
 def test_cast_full_size_64M(src, mode):
-    """BASELINE cast config at full size (64M elements, 1% outliers, 0.01%
+    """The cast benchmark configuration at full size (64M elements, 1% outliers, 0.01%
     NaN/Inf): every byte equal to an independent torch restatement of the
     recipe on the GPU, with NaN inputs checked against the pinned +FMAX code."""
     b2x = _b2x()

@@ -1,6 +1,6 @@
 """GPU parity of the tcgen05 fp8 GEMM (libb2x) against the float64 CPU oracle.
 
-Tolerance: max |C - C_ref| <= 1e-2 * ||A|| * ||B|| / sqrt(K),
+Tolerance (the accuracy target of this path): max |C - C_ref| <= 1e-2 * ||A|| * ||B|| / sqrt(K),
 with ||A|| the largest row 2-norm of the dequantized A and ||B|| the largest
 column 2-norm of the dequantized B, on top of the rounding of C to bf16
 (2^-8 * |C_ref| per element; fp8_oracle.gemm_error).  Split-K must agree with
@@ -149,7 +149,7 @@ def test_small_m_paths(M, split_k, b_layout):
 
 
 def test_splitk_decode_shape_full():
-    """BASELINE config: M=64 N=8192 K=28672, SPLIT_K=8, per-tensor e4m3, bf16 out.
+    """Decode benchmark configuration: M=64 N=8192 K=28672, SPLIT_K=8, per-tensor e4m3, bf16 out.
     Checked against the oracle on a sample of 512 output columns."""
     M, N, K = 64, 8192, 28672
     a, sa = _quant((M, K), O.E4M3, 9)
@@ -165,7 +165,7 @@ def test_splitk_decode_shape_full():
 
 
 def test_gemm_512_config0():
-    """512^3, A,B ~N(0,1) per-tensor e4m3, bf16 out."""
+    """The CPU-runnable benchmark configuration: 512^3, A,B ~N(0,1) per-tensor e4m3, bf16 out."""
     a, sa = _quant((512, 512), O.E4M3, 0)
     b, sb = _quant((512, 512), O.E4M3, 1)
     ref = O.gemm(a, b, scale_mode="tensor", scale_a=sa, scale_b=sb)
@@ -220,7 +220,7 @@ def test_blockscaled_vs_oracle(shape):
 
 
 def test_blockscaled_config2_sampled():
-    """4096 x 7168 x 7168, A 1x128 scales, B 128x128 scales."""
+    """The block-scaled benchmark configuration: 4096 x 7168 x 7168, A 1x128 scales, B 128x128 scales."""
     b2x = _b2x()
     M, N, K = 4096, 7168, 7168
     g = torch.Generator(device="cuda").manual_seed(2)

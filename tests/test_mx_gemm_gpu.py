@@ -91,7 +91,7 @@ def test_mx_gemm_matches_gpu_cast_scales():
 
 
 def test_mx_gemm_large_sampled():
-    """4096 x 7168 x 7168 (the block-scaled BASELINE shape) in MX form, checked
+    """4096 x 7168 x 7168 (the block-scaled benchmark shape) in MX form, checked
     on a sample of rows against the oracle."""
     import b2x
     M, N, K = 4096, 7168, 7168

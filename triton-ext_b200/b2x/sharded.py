@@ -1,6 +1,6 @@
 """Multi-GPU partitioning of fp8 linear layers (one process per GPU).
 
-The reference has no multi-GPU code; the BASELINE layer set (Llama-3-70B
+The reference has no multi-GPU code; the benchmark's layer set (Llama-3-70B
 shapes at 8192 tokens) is partitioned the way tensor-parallel MLP/attention
 projections are:
 
