@@ -92,6 +92,26 @@ def test_no_cpu_fallback():
         b2x.matmul(a, a.t(), {})
 
 
+def test_new_ops_have_no_cpu_fallback():
+    a = torch.zeros(4, 16, dtype=torch.float8_e4m3fn)
+    w = torch.zeros(256, 16, dtype=torch.float8_e4m3fn)
+    with pytest.raises(ValueError, match="CUDA"):
+        b2x.grouped_gemm([a], [a])
+    with pytest.raises(ValueError, match="CUDA"):
+        b2x.gemm_swiglu(a, w)
+    with pytest.raises(ValueError, match="CUDA"):
+        b2x.stoch_round(torch.zeros(8), torch.bfloat16, torch.zeros(8, dtype=torch.int32))
+
+
+def test_mx_scale_mode_and_config_mapping():
+    sa = torch.zeros(4, 4, dtype=torch.uint8)
+    assert G._scale_mode(sa, sa) == "mx"
+    with pytest.raises(ValueError):
+        G._scale_mode(sa, torch.zeros(4, 4))  # MX scales must both be uint8
+    assert G._to_b2x_config({"BLOCK_SIZE_N": 192}, 1024)[1] == 192  # the MX tile width is kept
+    assert G._to_b2x_config({"BLOCK_SIZE_N": 200}, 1024)[1] == 256  # other widths snap to 64/128/256
+
+
 def test_matmul_reference_asserts():
     a = torch.zeros(4, 16, dtype=torch.float8_e4m3fn)
     with pytest.raises(AssertionError, match="Incompatible dimensions"):
