@@ -367,3 +367,27 @@ def stoch_round(x: np.ndarray, r: np.ndarray, fmt: str) -> np.ndarray:
     hi = (yb >> 16).astype(np.uint16)
     hi = np.where(sat, ((yb >> 16) & 0x8000) | 0x7F7F, hi)
     return np.where(np.isnan(y), np.uint16(0x7FFF), hi).astype(np.uint16)
+
+
+# ----------------------------------------------------------------------------
+# Split-K reduction of a reference-layout workspace.
+
+
+def reduce_k(ws: np.ndarray, M: int, N: int, split_k: int, out: str = "f32") -> np.ndarray:
+    """c[m, n] = sum over s = 0..SPLIT_K-1, in that order, of ws[s*M + m, n],
+    accumulated in fp32 and stored in `out` ("f32", "bf16" bits as uint16,
+    "f16" bits as uint16) with round-to-nearest-even -- the reference's
+    `_reduce_k_kernel` (extensions/utlx/tlx/tutorials/blackwell_gemm_ws.py:
+    1033-1056: acc = 0; acc += partial.to(fp32) per split; acc.to(OUTPUT_DTYPE)).
+    `ws` holds float32 values (already widened from the workspace dtype)."""
+    w = np.asarray(ws, np.float32).reshape(split_k, M, N)
+    acc = np.zeros((M, N), np.float32)
+    for s in range(split_k):
+        acc = (acc + w[s]).astype(np.float32)
+    if out == "f32":
+        return acc
+    if out == "bf16":
+        return (bf16_round(acc).view(np.uint32) >> 16).astype(np.uint16)
+    if out == "f16":
+        return acc.astype(np.float16).view(np.uint16)
+    raise ValueError(out)
