@@ -268,9 +268,10 @@ def stoch_round_gbs(dev="cuda", iters=20):
     x = torch.randn((8192, n // 8192), device=dev, generator=g)
     r = torch.randint(-2 ** 31, 2 ** 31 - 1, x.shape, device=dev, dtype=torch.int32, generator=g)
     out = {}
-    for name, dt, nb in (("e4m3", torch.float8_e4m3fn, 1), ("bf16", torch.bfloat16, 2)):
-        ms = graph_ms(lambda: b2x.stoch_round(x, dt, r), iters)  # noqa: B023
-        out[name] = round(n * (8 + nb) / (ms * 1e-3) / 1e9, 1)
+    for rounding in ("rs", "exact32"):
+        for name, dt, nb in (("e4m3", torch.float8_e4m3fn, 1), ("bf16", torch.bfloat16, 2)):
+            ms = graph_ms(lambda: b2x.stoch_round(x, dt, r, rounding=rounding), iters)  # noqa: B023
+            out[f"{rounding}_{name}" if rounding != "rs" else name] = round(n * (8 + nb) / (ms * 1e-3) / 1e9, 1)
     return out
 
 

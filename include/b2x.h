@@ -132,13 +132,35 @@ B2X_API b2x_status b2x_amax(const void* x, b2x_dtype x_type, int64_t rows, int64
 B2X_API b2x_status b2x_stoch_round(const float* x, int64_t rows, int64_t cols, int64_t ld_x, const uint32_t* rbits,
                                    int64_t ld_r, void* y, b2x_dtype y_type, int64_t ld_y, void* stream);
 
+/*
+ * Stochastic rounding with the hardware instruction the reference's lowering
+ * emits, cvt.rs.satfinite (extensions/utlx/test/test_tlx.py:5182 asserts it;
+ * the rounding mode "rs" is chosen in extensions/utlx/ops/NewOps.cpp:249-303).
+ * Same arguments as b2x_stoch_round.  The instruction rounds a pack of 4
+ * (e4m3 / e5m2) or 2 (fp16 / bf16) values with one 32-bit entropy word split
+ * into per-lane fields.  Packs are consecutive columns of a row starting at
+ * column 0; a pack takes the rbits word of its first element and ignores the
+ * others (how the reference's Triton lowering folds per-element words into a
+ * pack is in Triton, outside the reference tree, so a bit-for-bit match with
+ * tlx.stoch_round for the same rand_bits is not claimed).  What the
+ * reference's tests check holds: representable values are unchanged, finite
+ * inputs give finite results next to the input, satfinite saturation, and
+ * different entropy gives different roundings.
+ * Replaces tlx.stoch_round(src, dst_ty, rand_bits) (utility.py:113-153).
+ */
+B2X_API b2x_status b2x_stoch_round_rs(const float* x, int64_t rows, int64_t cols, int64_t ld_x, const uint32_t* rbits,
+                                      int64_t ld_r, void* y, b2x_dtype y_type, int64_t ld_y, void* stream);
+
 /* ------------------------------------------------------------------ GEMM */
 
 /*
  * Tile / pipeline configuration.  Same keys as the reference's config dict
  * (blackwell_gemm_ws.py:1097-1109); zero means "pick".  NUM_MMA_GROUPS,
- * NUM_CTAS and INTERLEAVE_EPILOGUE are accepted for drop-in compatibility:
- * this build's CTA tile is always one 128-row tcgen05 MMA group on one SM.
+ * NUM_CTAS and INTERLEAVE_EPILOGUE are accepted for drop-in compatibility.
+ * Each CTA owns 128 rows of the output tile.  num_ctas = 2 runs the paired
+ * kernel: two CTAs of a cluster share 256 x 256 tiles through cta_group::2
+ * MMAs (each loads its own half of A and of B, no multicast); num_ctas = 1
+ * runs single-CTA 128 x block_n tiles; 0 lets the library choose.
  */
 typedef struct {
   int block_m, block_n, block_k;

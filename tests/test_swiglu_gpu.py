@@ -1,11 +1,14 @@
 """GPU check of the gate+up GEMM fused with SwiGLU and fp8 quantization
 (b2x.gemm_swiglu, C ABI b2x_fp8_gemm_swiglu) against the float64 oracle:
 h_ref = silu(g) * u from the oracle GEMMs of the gate and up halves.
-Floating-point tolerances (h passes through exp and an fp8 rounding):
-  block 1x128 scales:  |s - amax_ref / 448| <= 1e-2 * s_ref + tiny
-  dequantized h:       |q * s - h_ref| <= 2^-3 |h_ref| + 2e-2 * amax_row(|h_ref|)
-(half an e4m3 ulp is 2^-4 |h|; the rest covers the GEMM's own error bound
-and the fast exp)."""
+Tolerances.  h differs from the float64 h_ref only by the fp32 accumulation
+order of the GEMM and the fast exp / division of silu (a few 1e-6 relative):
+  scales (1x128 block scales, and the amax of the given-scale mode):
+      |s - s_ref| <= 1e-5 * s_ref
+  fp8 codes: q must equal the oracle's quantization of h_ref with the kernel's
+      own scale, byte for byte, except that a neighbouring code (one step) is
+      accepted where h_ref * inv lies within 1e-3 relative of the rounding
+      boundary between the two codes."""
 import numpy as np
 import pytest
 import torch
@@ -32,6 +35,25 @@ def _h_ref(qx, sx, qg, sg, qu, su):
     return g / (1.0 + np.exp(-g)) * u
 
 
+def _check_codes(q, y):
+    """q: the kernel's e4m3 bytes; y: h_ref times the kernel's inverse scale."""
+    yc = np.clip(y, -448.0, 448.0)
+    want = O.f32_to_fp8_bits(yc.astype(np.float32), O.E4M3)
+    diff = q != want
+    if not diff.any():
+        return
+    vq = O.fp8_bits_to_f64(q[diff], O.E4M3)
+    vw = O.fp8_bits_to_f64(want[diff], O.E4M3)
+    yd = yc[diff]
+    # neighbouring codes: same sign, magnitudes one code apart
+    one_step = ((q[diff] & 0x80) == (want[diff] & 0x80)) & (np.abs((q[diff] & 0x7F).astype(int) -
+                                                                      (want[diff] & 0x7F).astype(int)) == 1)
+    near = np.abs((vq + vw) / 2 - yd) <= 1e-3 * np.abs(yd)
+    bad = ~(one_step & near)
+    assert not bad.any(), (f"{bad.sum()} of {q.size} codes differ beyond a boundary case; first: "
+                           f"got {vq[bad][0]} want {vw[bad][0]} y {yd[bad][0]}")
+
+
 def _run(M, I, K, mode, seed=0):
     import b2x
     qx, sx, qg, sg, qu, su = _operands(M, I, K, seed)
@@ -47,26 +69,26 @@ def _run(M, I, K, mode, seed=0):
     W = b2x.interleave_gate_up(Wg, Wu)
     tsx, tsw = torch.tensor([sx], device="cuda"), torch.tensor([sw], device="cuda")
     href = _h_ref(qx, sx, qg, sg, qu, su)
-    amax_row = np.abs(href).max(axis=1, keepdims=True)
     before = b2x.launch_count()
     if mode == "block1x128":
         h, s = b2x.gemm_swiglu(X, W, tsx, tsw)
         torch.cuda.synchronize()
         s = s.cpu().numpy()
         sref = np.abs(href).reshape(M, I // 128, 128).max(axis=2) / 448.0
-        assert np.all(np.abs(s - sref) <= 1e-2 * sref + 1e-30), np.abs(s - sref).max()
-        deq = O.fp8_bits_to_f64(h.view(torch.uint8).cpu().numpy(), O.E4M3) * np.repeat(s, 128, axis=1)
+        assert np.all(np.abs(s - sref) <= 1e-5 * sref + 1e-30), (np.abs(s - sref) / sref).max()
+        inv = np.where(s == 0, 0.0, 1.0 / s.astype(np.float64))
+        _check_codes(h.view(torch.uint8).cpu().numpy(), href * np.repeat(inv, 128, axis=1))
     else:
         given = float(np.abs(href).max() / 448.0 * 1.25)
         amax = torch.zeros(1, device="cuda")
         h, _ = b2x.gemm_swiglu(X, W, tsx, tsw, mode="given", h_scale=torch.tensor([given], device="cuda"),
                                h_amax=amax)
         torch.cuda.synchronize()
-        assert abs(amax.item() - np.abs(href).max()) <= 1e-2 * np.abs(href).max()
-        deq = O.fp8_bits_to_f64(h.view(torch.uint8).cpu().numpy(), O.E4M3) * np.float64(np.float32(given))
+        assert abs(amax.item() - np.abs(href).max()) <= 1e-5 * np.abs(href).max()
+        inv = 1.0 / np.float64(np.float32(given))
+        _check_codes(h.view(torch.uint8).cpu().numpy(), href * inv)
     assert b2x.launch_count() == before + 1, "expected one fused kernel launch"
-    err = np.abs(deq - href) - (2.0 ** -3) * np.abs(href) - 2e-2 * amax_row
-    assert err.max() <= 0, f"{M}x{I}x{K} {mode}: worst excess {err.max():.4g}"
+
 
 
 @pytest.mark.parametrize("M,I,K", [(256, 256, 512), (512, 384, 1024), (200, 128, 256), (64, 256, 384)])

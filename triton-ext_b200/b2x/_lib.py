@@ -27,7 +27,7 @@ EXPORTED = (
     "b2x_gemm_workspace_size", "b2x_fp8_gemm", "b2x_splitk_reduce", "b2x_last_error",
     "b2x_read_device_status", "b2x_abi_version", "b2x_launch_count", "b2x_fp8_gemm_splitk_noalloc",
     "b2x_trace_read", "b2x_allreduce_signal_words", "b2x_fp8_gemm_allreduce",
-    "b2x_stoch_round", "b2x_grouped_gemm_workspace_size", "b2x_fp8_grouped_gemm", "b2x_fp8_gemm_swiglu",
+    "b2x_stoch_round", "b2x_stoch_round_rs", "b2x_grouped_gemm_workspace_size", "b2x_fp8_grouped_gemm", "b2x_fp8_gemm_swiglu",
 )
 
 AR_MAX_RANKS = 8
@@ -141,6 +141,8 @@ def lib() -> ctypes.CDLL:
         L.b2x_stoch_round.argtypes = [ctypes.c_void_p, ctypes.c_int64, ctypes.c_int64, ctypes.c_int64, ctypes.c_void_p,
                                        ctypes.c_int64, ctypes.c_void_p, ctypes.c_int, ctypes.c_int64, ctypes.c_void_p]
         L.b2x_stoch_round.restype = ctypes.c_int
+        L.b2x_stoch_round_rs.argtypes = L.b2x_stoch_round.argtypes
+        L.b2x_stoch_round_rs.restype = ctypes.c_int
         L.b2x_allreduce_signal_words.argtypes = [ctypes.c_int64, ctypes.c_int64]
         L.b2x_allreduce_signal_words.restype = ctypes.c_size_t
         L.b2x_fp8_gemm_allreduce.argtypes = [ctypes.POINTER(GemmArgs), ctypes.POINTER(AllReduceArgs), ctypes.c_void_p]
@@ -182,7 +184,19 @@ def read_trace(max_ctas: int = 148):
     return buf[: n.value]
 
 
+# Called with the status whenever read_device_status() finds a kernel that
+# gave up a bounded wait: state that such a kernel may have left half-updated
+# (the cached split-K workspaces, for one) registers a hook to drop it.
+_status_hooks: list = []
+
+
 def read_device_status() -> int:
+    """Reads and clears the current device's status word (blocking).  A
+    nonzero value means a kernel gave up a bounded wait; the registered
+    hooks then drop any state that kernel may have left dirty."""
     v = ctypes.c_int(0)
     check(lib().b2x_read_device_status(ctypes.byref(v)))
+    if v.value:
+        for hook in list(_status_hooks):
+            hook(v.value)
     return v.value

@@ -48,7 +48,9 @@ def _require_cuda(*ts: torch.Tensor) -> None:
 # ----------------------------------------------------------------------------
 # Workspaces.  Split-K workspaces must be all-zero before a call and are
 # returned all-zero by every successful call, so one zeroed buffer per
-# (device, stream) is reused; it is dropped after any failed call.
+# (device, stream) is reused; it is dropped after any failed call and
+# whenever the device status word reports a kernel that gave up a wait (its
+# partial sums and tile counters may be left nonzero).
 
 _ws_lock = threading.Lock()
 _ws_cache: dict = {}
@@ -64,9 +66,12 @@ def _workspace(dev: torch.device, nbytes: int, zeroed: bool) -> torch.Tensor:
         return buf
 
 
-def _drop_workspaces() -> None:
+def _drop_workspaces(_status: int = 0) -> None:
     with _ws_lock:
         _ws_cache.clear()
+
+
+L._status_hooks.append(_drop_workspaces)
 
 
 # ----------------------------------------------------------------------------
@@ -343,9 +348,12 @@ SR_DTYPES = {torch.float8_e4m3fn: L.E4M3, torch.float8_e5m2: L.E5M2, torch.float
 
 
 @torch.library.custom_op("b2x::stoch_round", mutates_args=())
-def stoch_round_op(src: torch.Tensor, dst_dtype: torch.dtype, rand_bits: torch.Tensor) -> torch.Tensor:
-    """fp32 -> e4m3 / e5m2 / fp16 / bf16 with one uint32 of entropy per
-    element; see include/b2x.h b2x_stoch_round."""
+def stoch_round_op(src: torch.Tensor, dst_dtype: torch.dtype, rand_bits: torch.Tensor,
+                   rounding: str = "rs") -> torch.Tensor:
+    """fp32 -> e4m3 / e5m2 / fp16 / bf16 with caller-given entropy;
+    rounding "rs" (b2x_stoch_round_rs) or "exact32" (b2x_stoch_round)."""
+    if rounding not in ("rs", "exact32"):
+        raise ValueError(f"rounding must be 'rs' or 'exact32', got {rounding!r}")
     _require_cuda(src, rand_bits)
     if src.dtype != torch.float32:
         raise TypeError(f"stoch_round takes a float32 source, got {src.dtype}")
@@ -366,25 +374,32 @@ def stoch_round_op(src: torch.Tensor, dst_dtype: torch.dtype, rand_bits: torch.T
     y = torch.empty((R, C), dtype=dst_dtype, device=src.device)
     if R * C:
         with torch.cuda.device(src.device):
-            L.check(L.lib().b2x_stoch_round(x.data_ptr(), R, C, x.stride(0), r.data_ptr(), r.stride(0),
-                                            y.data_ptr(), SR_DTYPES[dst_dtype], C,
-                                            ctypes.c_void_p(_stream(src.device))))
+            fn = L.lib().b2x_stoch_round_rs if rounding == "rs" else L.lib().b2x_stoch_round
+            L.check(fn(x.data_ptr(), R, C, x.stride(0), r.data_ptr(), r.stride(0), y.data_ptr(), SR_DTYPES[dst_dtype],
+                       C, ctypes.c_void_p(_stream(src.device))))
     return y.reshape(shape)
 
 
 @stoch_round_op.register_fake
-def _(src, dst_dtype, rand_bits):
+def _(src, dst_dtype, rand_bits, rounding="rs"):
     return src.new_empty(src.shape, dtype=dst_dtype)
 
 
-def stoch_round(src: torch.Tensor, dst_ty: torch.dtype, rand_bits: torch.Tensor) -> torch.Tensor:
-    """Stochastic rounding of float32 `src` to `dst_ty` with one uint32 of
-    entropy per element (the reference's tlx.stoch_round(src, dst_ty,
-    rand_bits), extensions/utlx/tlx/language/tlx/utility.py:113-153).
+def stoch_round(src: torch.Tensor, dst_ty: torch.dtype, rand_bits: torch.Tensor, *,
+                rounding: str = "rs") -> torch.Tensor:
+    """Stochastic rounding of float32 `src` to `dst_ty` (the reference's
+    tlx.stoch_round(src, dst_ty, rand_bits), extensions/utlx/tlx/language/
+    tlx/utility.py:113-153).  rand_bits has src's shape.
+
+    rounding="rs" (default): the hardware `cvt.rs.satfinite` the reference
+    lowers to; packs of 4 (fp8) / 2 (16-bit) consecutive elements of a row
+    share the rand_bits word of the pack's first element.
+    rounding="exact32": b2x's integer rule, every element rounds up with
+    probability frac/2^32 from its own full word (bit-exact CPU oracle).
     Same-dtype requests return `src` unchanged, as the reference does."""
     if dst_ty == src.dtype:
         return src
-    return torch.ops.b2x.stoch_round(src, dst_ty, rand_bits)
+    return torch.ops.b2x.stoch_round(src, dst_ty, rand_bits, rounding)
 
 
 # ----------------------------------------------------------------------------

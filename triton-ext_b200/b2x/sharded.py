@@ -81,6 +81,15 @@ class FusedRowParallel:
 
     mode: "auto" (multicast when the group supports it, else peer loads and
     stores), "multicast" or "peer".
+
+    Failure handling: the kernel's waits for peers are bounded (10 s).  A
+    wait that gives up records a timeout in the device status word and can
+    leave the arrival counters of the signal buffer partly counted, which a
+    later call would misread.  `check()` (collective: every rank calls it)
+    reads the status on every rank and, if any rank timed out, zeroes the
+    signal buffers everywhere, restarts the epoch and raises B2XError.
+    `reset()` does the clearing alone; it also runs, collectively, before the
+    32-bit epoch would wrap.
     """
 
     def __init__(self, M: int, N: int, device, group=None, mode: str = "auto"):
@@ -146,13 +155,40 @@ class FusedRowParallel:
             if len(self._plans) > 64:
                 self._plans.clear()
             self._plans[key] = g
+        if self.epoch >= 0xFFFFFFFF:
+            self.reset()  # every rank reaches this call at the same count
         self.epoch += 1
-        self._ar.epoch = self.epoch & 0xFFFFFFFF or 1
+        self._ar.epoch = self.epoch
         with torch.cuda.device(self.device):
             st = L.lib().b2x_fp8_gemm_allreduce(ctypes.byref(g), ctypes.byref(self._ar),
                                                 ctypes.c_void_p(torch.cuda.current_stream(self.device).cuda_stream))
         L.check(st)
         return self.out
+
+
+    def reset(self) -> None:
+        """Collective: zero the signal buffer on every rank and restart the
+        epoch.  No fused call may be in flight on any rank."""
+        torch.cuda.synchronize(self.device)
+        dist.barrier(self.group)
+        self.signal.zero_()
+        torch.cuda.synchronize(self.device)
+        dist.barrier(self.group)
+        self.epoch = 0
+
+    def check(self) -> None:
+        """Collective: raise B2XError (after reset()) if a fused call on any
+        rank gave up waiting for its peers since the last check."""
+        from . import _lib as L
+        with torch.cuda.device(self.device):
+            torch.cuda.synchronize(self.device)
+            st = L.read_device_status()
+        flag = torch.tensor([st], dtype=torch.int64, device=self.device)
+        dist.all_reduce(flag, op=dist.ReduceOp.MAX, group=self.group)
+        if flag.item():
+            self.reset()
+            raise L.B2XError(L.ERR_TIMEOUT, f"fused all-reduce: a rank gave up waiting for its peers "
+                                            f"(device status 0x{int(flag.item()):x}); signal buffers were reset")
 
 
 class LlamaFP8LinearSet:

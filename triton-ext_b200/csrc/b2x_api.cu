@@ -698,25 +698,36 @@ b2x_status b2x_fp8_gemm_allreduce(const b2x_gemm_args* args, const b2x_allreduce
   return fp8_gemm_impl(&a, &ar, stream);
 }
 
-b2x_status b2x_stoch_round(const float* x, int64_t rows, int64_t cols, int64_t ld_x, const uint32_t* rbits,
-                           int64_t ld_r, void* y, b2x_dtype y_type, int64_t ld_y, void* stream) {
+static b2x_status stoch_round_impl(const char* who, int rs, const float* x, int64_t rows, int64_t cols, int64_t ld_x,
+                                   const uint32_t* rbits, int64_t ld_r, void* y, b2x_dtype y_type, int64_t ld_y,
+                                   void* stream) {
   t_err[0] = 0;
   if (y_type != B2X_E4M3 && y_type != B2X_E5M2 && y_type != B2X_F16 && y_type != B2X_BF16)
-    return fail(B2X_ERR_UNSUPPORTED, "b2x_stoch_round: target must be e4m3, e5m2, fp16 or bf16 (got %d)", (int)y_type);
-  if (rows < 0 || cols < 0) return fail(B2X_ERR_INVALID_ARG, "b2x_stoch_round: negative shape");
+    return fail(B2X_ERR_UNSUPPORTED, "%s: target must be e4m3, e5m2, fp16 or bf16 (got %d)", who, (int)y_type);
+  if (rows < 0 || cols < 0) return fail(B2X_ERR_INVALID_ARG, "%s: negative shape", who);
   if (rows == 0 || cols == 0) return B2X_OK;
-  if (!x || !rbits || !y) return fail(B2X_ERR_INVALID_ARG, "b2x_stoch_round: NULL pointer");
+  if (!x || !rbits || !y) return fail(B2X_ERR_INVALID_ARG, "%s: NULL pointer", who);
   if (ld_x < cols || ld_r < cols || ld_y < cols)
-    return fail(B2X_ERR_INVALID_ARG, "b2x_stoch_round: a row stride is smaller than cols");
+    return fail(B2X_ERR_INVALID_ARG, "%s: a row stride is smaller than cols", who);
   const int out_bytes = (y_type == B2X_E4M3 || y_type == B2X_E5M2) ? 1 : 2;
   if (((uintptr_t)x % 4) || ((uintptr_t)rbits % 4) || ((uintptr_t)y % out_bytes))
-    return fail(B2X_ERR_INVALID_ARG, "b2x_stoch_round: misaligned pointer");
+    return fail(B2X_ERR_INVALID_ARG, "%s: misaligned pointer", who);
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
-  e = launch_stoch_round(x, rbits, y, y_type, rows, cols, ld_x, ld_r, ld_y, device_num_sms(dev), (cudaStream_t)stream);
-  if (e != cudaSuccess) return cuda_fail(e, "b2x_stoch_round launch");
+  e = launch_stoch_round(x, rbits, y, y_type, rows, cols, ld_x, ld_r, ld_y, device_num_sms(dev), (cudaStream_t)stream, rs);
+  if (e != cudaSuccess) return cuda_fail(e, who);
   return B2X_OK;
+}
+
+b2x_status b2x_stoch_round(const float* x, int64_t rows, int64_t cols, int64_t ld_x, const uint32_t* rbits,
+                           int64_t ld_r, void* y, b2x_dtype y_type, int64_t ld_y, void* stream) {
+  return stoch_round_impl("b2x_stoch_round", 0, x, rows, cols, ld_x, rbits, ld_r, y, y_type, ld_y, stream);
+}
+
+b2x_status b2x_stoch_round_rs(const float* x, int64_t rows, int64_t cols, int64_t ld_x, const uint32_t* rbits,
+                              int64_t ld_r, void* y, b2x_dtype y_type, int64_t ld_y, void* stream) {
+  return stoch_round_impl("b2x_stoch_round_rs", 1, x, rows, cols, ld_x, rbits, ld_r, y, y_type, ld_y, stream);
 }
 
 b2x_status b2x_trace_read(uint64_t* out, int max_ctas, int* n_ctas) {

@@ -80,7 +80,7 @@ cudaError_t launch_fp8_gemm_blockscaled(const GemmLaunch& g, cudaStream_t st);
 cudaError_t launch_fp8_gemm_mx(const GemmLaunch& g, cudaStream_t st);
 size_t mx_workspace_bytes(int64_t M, int64_t N, int64_t K, int bn);
 cudaError_t launch_stoch_round(const float* x, const uint32_t* r, void* y, b2x_dtype yt, int64_t rows, int64_t cols,
-                               int64_t ld_x, int64_t ld_r, int64_t ld_y, int num_sms, cudaStream_t st);
+                               int64_t ld_x, int64_t ld_r, int64_t ld_y, int num_sms, cudaStream_t st, int rs);
 cudaError_t launch_splitk_reduce(const void* ws, b2x_dtype wt, void* c, b2x_dtype ct, int64_t M, int64_t N,
                                  int64_t ldc, int split_k, cudaStream_t st);
 

@@ -21,6 +21,14 @@
 // properties -- exact values unchanged, no NaN/Inf from finite inputs, results
 // next to the input -- which this rule keeps with every element's full word.
 //
+// Second mode, RS (b2x_stoch_round_rs): the hardware instruction the
+// reference's lowering emits, `cvt.rs.satfinite.{e4m3x4,e5m2x4,f16x2,bf16x2}.f32`
+// (the reference test asserts it in the PTX, test_tlx.py:5182).  It rounds a
+// pack of 4 (fp8) or 2 (16-bit) values with ONE 32-bit entropy word whose
+// fields feed the lanes.  Packs are consecutive columns of a row starting at
+// column 0, and a pack takes the word of its first element (the other words
+// of the pack are not read).  The rounding itself is the instruction's.
+//
 // The kernel is HBM-bound: 4 + 4 bytes in and 1 (fp8) or 2 bytes out per
 // element; a thread handles 8 consecutive elements per step (two 16-byte
 // loads of x and of r).
@@ -81,6 +89,57 @@ __device__ __forceinline__ uint32_t sr_magnitude(uint32_t abits, uint32_t r, SrF
   // exact value q * 2^u in fp32 (q < 2^25, 2^u >= 2^-133 for all targets)
   const float pw = u >= -126 ? __uint_as_float((uint32_t)(u + 127) << 23) : __uint_as_float(1u << (u + 149));
   return __float_as_uint((float)q * pw);
+}
+
+// Hardware stochastic rounding of a pack: x[0] lands in the lowest byte /
+// half of the result (the instruction puts its first operand in the highest).
+template <int T>
+__device__ __forceinline__ uint32_t cvt_rs_pack(const float* x, uint32_t r) {
+  uint32_t o;
+  if constexpr (T == B2X_E4M3)
+    asm("cvt.rs.satfinite.e4m3x4.f32 %0, {%1, %2, %3, %4}, %5;"
+        : "=r"(o) : "f"(x[3]), "f"(x[2]), "f"(x[1]), "f"(x[0]), "r"(r));
+  else if constexpr (T == B2X_E5M2)
+    asm("cvt.rs.satfinite.e5m2x4.f32 %0, {%1, %2, %3, %4}, %5;"
+        : "=r"(o) : "f"(x[3]), "f"(x[2]), "f"(x[1]), "f"(x[0]), "r"(r));
+  else if constexpr (T == B2X_BF16)
+    asm("cvt.rs.satfinite.bf16x2.f32 %0, %1, %2, %3;" : "=r"(o) : "f"(x[1]), "f"(x[0]), "r"(r));
+  else
+    asm("cvt.rs.satfinite.f16x2.f32 %0, %1, %2, %3;" : "=r"(o) : "f"(x[1]), "f"(x[0]), "r"(r));
+  return o;
+}
+
+template <int T>
+constexpr int rs_pack() {
+  return (T == B2X_E4M3 || T == B2X_E5M2) ? 4 : 2;
+}
+
+// Eight consecutive elements starting at a pack boundary (RS mode).
+template <int T>
+__device__ __forceinline__ void rs8(const float (&x)[8], const uint32_t (&r)[8], void* dst) {
+  constexpr int P = rs_pack<T>();
+  uint32_t w[8 / P];
+#pragma unroll
+  for (int k = 0; k < 8 / P; ++k) w[k] = cvt_rs_pack<T>(x + k * P, r[k * P]);
+  if constexpr (P == 4)
+    *reinterpret_cast<uint2*>(dst) = make_uint2(w[0], w[1]);
+  else
+    *reinterpret_cast<uint4*>(dst) = make_uint4(w[0], w[1], w[2], w[3]);
+}
+
+// One element of column c (RS mode): it is placed in its lane of the pack,
+// the other lanes hold zero, and the pack's word is its first element's.
+template <int T>
+__device__ __forceinline__ void rs1(float x, const uint32_t* r_row, int64_t c, uint8_t* dst) {
+  constexpr int P = rs_pack<T>();
+  const int lane = (int)(c % P);
+  float v[4] = {0.f, 0.f, 0.f, 0.f};
+  v[lane] = x;
+  const uint32_t o = cvt_rs_pack<T>(v, r_row[c - lane]);
+  if constexpr (P == 4)
+    *dst = (uint8_t)(o >> (8 * lane));
+  else
+    *reinterpret_cast<uint16_t*>(dst) = (uint16_t)(o >> (16 * lane));
 }
 
 // Round each element, then encode.  The product of a small integer and a
@@ -149,7 +208,7 @@ struct SrArgs {
   int64_t vec_per_row;                   // cols / 8 when every row start is 16-byte aligned, else 0
 };
 
-template <int T>
+template <int T, int RS>
 __global__ void __launch_bounds__(256) stoch_round_kernel(const SrArgs a) {
   constexpr int kOut = (T == B2X_E4M3 || T == B2X_E5M2) ? 1 : 2;
   const int64_t stride = (int64_t)gridDim.x * blockDim.x;
@@ -165,7 +224,10 @@ __global__ void __launch_bounds__(256) stoch_round_kernel(const SrArgs a) {
       const uint4 r0 = __ldcs(rp), r1 = __ldcs(rp + 1);
       const float xs[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
       const uint32_t rs[8] = {r0.x, r0.y, r0.z, r0.w, r1.x, r1.y, r1.z, r1.w};
-      sr8<T>(xs, rs, a.y + (row * a.ld_y + c) * kOut);
+      if constexpr (RS)
+        rs8<T>(xs, rs, a.y + (row * a.ld_y + c) * kOut);
+      else
+        sr8<T>(xs, rs, a.y + (row * a.ld_y + c) * kOut);
     }
     // columns past the last full group of 8
     const int64_t tail0 = a.vec_per_row * 8;
@@ -173,20 +235,26 @@ __global__ void __launch_bounds__(256) stoch_round_kernel(const SrArgs a) {
     for (int64_t i = tid; i < ntail; i += stride) {
       const int64_t row = i / (a.cols - tail0);
       const int64_t c = tail0 + (i - row * (a.cols - tail0));
-      sr1<T>(a.x[row * a.ld_x + c], a.r[row * a.ld_r + c], a.y + (row * a.ld_y + c) * kOut);
+      if constexpr (RS)
+        rs1<T>(a.x[row * a.ld_x + c], a.r + row * a.ld_r, c, a.y + (row * a.ld_y + c) * kOut);
+      else
+        sr1<T>(a.x[row * a.ld_x + c], a.r[row * a.ld_r + c], a.y + (row * a.ld_y + c) * kOut);
     }
   } else {
     const int64_t n = a.rows * a.cols;
     for (int64_t i = tid; i < n; i += stride) {
       const int64_t row = i / a.cols;
       const int64_t c = i - row * a.cols;
-      sr1<T>(a.x[row * a.ld_x + c], a.r[row * a.ld_r + c], a.y + (row * a.ld_y + c) * kOut);
+      if constexpr (RS)
+        rs1<T>(a.x[row * a.ld_x + c], a.r + row * a.ld_r, c, a.y + (row * a.ld_y + c) * kOut);
+      else
+        sr1<T>(a.x[row * a.ld_x + c], a.r[row * a.ld_r + c], a.y + (row * a.ld_y + c) * kOut);
     }
   }
 }
 
 cudaError_t launch_stoch_round(const float* x, const uint32_t* r, void* y, b2x_dtype yt, int64_t rows, int64_t cols,
-                               int64_t ld_x, int64_t ld_r, int64_t ld_y, int num_sms, cudaStream_t st) {
+                               int64_t ld_x, int64_t ld_r, int64_t ld_y, int num_sms, cudaStream_t st, int rs) {
   SrArgs a;
   a.x = x;
   a.r = r;
@@ -205,11 +273,20 @@ cudaError_t launch_stoch_round(const float* x, const uint32_t* r, void* y, b2x_d
   const int64_t cap = (int64_t)num_sms * 8;  // 8 resident 256-thread CTAs per SM
   if (blocks > cap) blocks = cap;
   if (blocks < 1) blocks = 1;
-  switch (yt) {
-    case B2X_E4M3: stoch_round_kernel<B2X_E4M3><<<(int)blocks, 256, 0, st>>>(a); break;
-    case B2X_E5M2: stoch_round_kernel<B2X_E5M2><<<(int)blocks, 256, 0, st>>>(a); break;
-    case B2X_F16: stoch_round_kernel<B2X_F16><<<(int)blocks, 256, 0, st>>>(a); break;
-    default: stoch_round_kernel<B2X_BF16><<<(int)blocks, 256, 0, st>>>(a); break;
+  if (rs) {
+    switch (yt) {
+      case B2X_E4M3: stoch_round_kernel<B2X_E4M3, 1><<<(int)blocks, 256, 0, st>>>(a); break;
+      case B2X_E5M2: stoch_round_kernel<B2X_E5M2, 1><<<(int)blocks, 256, 0, st>>>(a); break;
+      case B2X_F16: stoch_round_kernel<B2X_F16, 1><<<(int)blocks, 256, 0, st>>>(a); break;
+      default: stoch_round_kernel<B2X_BF16, 1><<<(int)blocks, 256, 0, st>>>(a); break;
+    }
+  } else {
+    switch (yt) {
+      case B2X_E4M3: stoch_round_kernel<B2X_E4M3, 0><<<(int)blocks, 256, 0, st>>>(a); break;
+      case B2X_E5M2: stoch_round_kernel<B2X_E5M2, 0><<<(int)blocks, 256, 0, st>>>(a); break;
+      case B2X_F16: stoch_round_kernel<B2X_F16, 0><<<(int)blocks, 256, 0, st>>>(a); break;
+      default: stoch_round_kernel<B2X_BF16, 0><<<(int)blocks, 256, 0, st>>>(a); break;
+    }
   }
   note_launch(1);
   return cudaGetLastError();
