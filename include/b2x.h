@@ -328,11 +328,15 @@ B2X_API b2x_status b2x_fp8_grouped_gemm(const b2x_gemm_group* groups, int num_gr
  * The signal buffer (b2x_allreduce_signal_words 32-bit words per rank, all
  * zero before the first call) carries the arrival and completion counts.
  * Every rank must make the same sequence of calls (same shapes, same
- * buffers), passing epoch = 1 on the first call after zeroing the signal
- * buffer and one more on each later call.  The kernel ends when the sum is
- * complete on this rank; a peer that never takes part makes it give up after
- * 10 s with B2X_ERR_TIMEOUT recorded in the device status word, after which
- * the signal buffers must be zeroed on every rank before the next call.
+ * buffers).  Calls are counted either by the caller, passing epoch = 1 on the
+ * first call after zeroing the signal buffer and one more on each later call
+ * (modulo 2^32, skipping 0), or, with epoch = 0 on every call, by the kernel
+ * itself in the signal buffer; the second form has no per-call argument, so
+ * the launch can be captured once in a CUDA graph and replayed.  The kernel
+ * ends when the sum is complete on this rank; a peer that never takes part
+ * makes it give up after 10 s with B2X_ERR_TIMEOUT recorded in the device
+ * status word, after which the signal buffers must be zeroed on every rank
+ * (and caller-kept epochs restarted) before the next call.
  * No counterpart in the reference, which has no multi-GPU code path; it
  * replaces, for the tensor-parallel layer set, a GEMM followed by an NCCL
  * all-reduce of its output.
@@ -344,7 +348,7 @@ typedef struct {
   void* c_peers[B2X_AR_MAX_RANKS];      /* C's buffer on each rank, as mapped in this process */
   void* signal_multicast;               /* multicast address of the signal buffer (with c_multicast) */
   void* signal_peers[B2X_AR_MAX_RANKS]; /* the signal buffer on each rank */
-  uint32_t epoch;                       /* 1, 2, 3, ... per call */
+  uint32_t epoch;                       /* 1, 2, 3, ... per call, or 0 on every call: counted on the device */
 } b2x_allreduce_args;
 
 B2X_API size_t b2x_allreduce_signal_words(int64_t M, int64_t N);

@@ -140,7 +140,6 @@ def test_allreduce_signal_words():
 @pytest.mark.parametrize("gemm_kw,ar_kw,status", [
     ({}, {"world": 9}, "ERR_INVALID_ARG"),
     ({}, {"rank": 2}, "ERR_INVALID_ARG"),
-    ({}, {"epoch": 0}, "ERR_INVALID_ARG"),
     ({"M": 384}, {}, "ERR_UNSUPPORTED"),                      # M not a multiple of 256
     ({"c_type": 2}, {}, "ERR_UNSUPPORTED"),                   # fp16 output
     ({"ldb_k": 256, "ldb_n": 1}, {}, "ERR_UNSUPPORTED"),      # row-major B

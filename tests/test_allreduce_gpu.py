@@ -97,8 +97,38 @@ def _worker(rank, world, port, q, cases):
                                 launched=launched, status=status,
                                 arrive_zero=bool((sig[64:64 + units] == 0).all()),
                                 done=int(sig[0]), done_expected=(call + 1) * units,
-                                finite=bool(np.isfinite(c).all())))
-            del fr
+                                calls_counted=int(sig[2]), finite=bool(np.isfinite(c).all())))
+            # the same call captured once in a CUDA graph and replayed: the
+            # kernel counts the calls itself, so every replay is a new call
+            qa, sa, qw, sw = _rank_inputs(M, N, Kr, rank, calls - 1, fmt_a, fmt_b, scaled)
+            A = torch.from_numpy(qa).to(dev).view(FP8[fmt_a])
+            W = torch.from_numpy(qw).to(dev).view(FP8[fmt_b])
+            tsa = torch.tensor([sa], device=dev) if scaled else None
+            tsw = torch.tensor([sw], device=dev) if scaled else None
+            torch.cuda.synchronize(dev)
+            dist.barrier()
+            s_cap = torch.cuda.Stream(dev)
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.stream(s_cap):
+                with torch.cuda.graph(graph, stream=s_cap):
+                    fr(A, tsa, W, tsw)
+            for rep in range(3):
+                fr.out.fill_(float("nan"))
+                torch.cuda.synchronize(dev)
+                dist.barrier()
+                graph.replay()
+                torch.cuda.synchronize(dev)
+                status = L.read_device_status()
+                c = fr.out.float().cpu().numpy()
+                ref, abs_parts, tol = _expected(M, N, Kr, world, calls - 1, fmt_a, fmt_b, scaled)
+                excess = float((np.abs(c - ref) - O.OUTPUT_ROUNDING * (np.abs(ref) + abs_parts)).max())
+                sig = fr.signal.cpu().numpy().astype(np.int64) & 0xFFFFFFFF
+                out.append(dict(case=(M, N, Kr, fr.mode, fmt_a, fmt_b, scaled, "graph"), call=calls + rep,
+                                err=(excess, float(tol)), launched=1, status=status,
+                                arrive_zero=bool((sig[64:64 + units] == 0).all()),
+                                done=int(sig[0]), done_expected=(calls + rep + 1) * units,
+                                calls_counted=int(sig[2]), finite=bool(np.isfinite(c).all())))
+            del graph, fr
         dist.barrier()
         dist.destroy_process_group()
         q.put((rank, out, None))
@@ -149,6 +179,7 @@ def _check(results):
                 assert excess <= tol, f"{what}: error {excess:.4g} > tol {tol:.4g}"
             assert rec["arrive_zero"], f"{what}: arrival counters not reset"
             assert rec["done"] == rec["done_expected"], f"{what}: done word {rec['done']} != {rec['done_expected']}"
+            assert rec["calls_counted"] == rec["call"] + 1, f"{what}: call count {rec['calls_counted']}"
 
 
 def test_fused_allreduce_modes_and_repeats():

@@ -51,6 +51,69 @@ def _worker(rank, world, port, q):
         q.put((rank, False, False, repr(e)))
 
 
+def _swiglu(x, w, sx, sw, h_scale, h_amax=None):
+    """float64 stand-in of gemm_swiglu on the interleaved gate/up weight."""
+    y = (x.double() @ w.double().t()) * float(sx) * float(sw)
+    y = y.reshape(y.shape[0], -1, 2, 128)
+    g, u = y[:, :, 0], y[:, :, 1]
+    h = (g * torch.sigmoid(g) * u).reshape(y.shape[0], -1)
+    if h_amax is not None:
+        h_amax.copy_(h.abs().max().float().reshape(1))
+    return h / float(h_scale)
+
+
+def _rand(shape, gen, device):
+    return torch.randn(shape, generator=gen, dtype=torch.float64), torch.tensor(0.5)
+
+
+def _chain_worker(rank, world, port, q):
+    try:
+        os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+        dist.init_process_group("gloo", rank=rank, world_size=world)
+        from b2x import sharded
+
+        class Small(sharded.LlamaFP8LinearSet):
+            SHAPES = {"qkv": (16, 64, 32), "gate_up": (16, 512, 32), "down": (16, 48, 256)}
+
+        ls = Small(rank, world, "cpu", tokens=16, mm=_mm, swiglu=_swiglu, make_input=_rand)
+        qo, h, d = ls.step()
+
+        def gather(t, dim):
+            parts = [torch.empty_like(t) for _ in range(world)]
+            dist.all_gather(parts, t.contiguous())
+            return torch.cat(parts, dim=dim)
+
+        wq, wgu, wd = gather(ls.wq, 0), gather(ls.wgu, 0), gather(ls.wd, 1)
+        ok_q = torch.allclose(gather(qo, 1), _mm(ls.x, wq, ls.sx, ls.sq, None), rtol=1e-12, atol=1e-10)
+        h_full = _swiglu(ls.x, wgu, ls.sx, ls.sgu, 1.0)
+        ok_h = torch.allclose(gather(h * ls.sh, 1), h_full, rtol=1e-12, atol=1e-10)
+        ok_d = torch.allclose(d, _mm(h_full, wd, 1.0, ls.sd, None), rtol=1e-10, atol=1e-9)
+        q.put((rank, bool(ok_q and ok_h and ok_d), (bool(ok_q), bool(ok_h), bool(ok_d))))
+        dist.barrier()
+        dist.destroy_process_group()
+    except Exception as e:  # pragma: no cover - reported to the parent
+        q.put((rank, False, repr(e)))
+
+
+def test_two_rank_chained_layer_set_matches_unsharded():
+    """LlamaFP8LinearSet on two gloo ranks with float64 stand-ins for the
+    kernels: gathered QKV and h shards, and the all-reduced down output,
+    equal the unsharded chain qkv = x.Wq^T, h = silu(x.Wg^T)*(x.Wu^T),
+    out = h.Wd^T."""
+    world = 2
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_chain_worker, args=(r, world, port, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    results = [q.get(timeout=120) for _ in range(world)]
+    for p in procs:
+        p.join(timeout=60)
+    for rank, ok, info in results:
+        assert ok, (rank, info)
+
+
 def test_two_rank_sharding_matches_unsharded():
     world = 2
     ctx = mp.get_context("spawn")

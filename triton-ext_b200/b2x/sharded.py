@@ -87,9 +87,10 @@ class FusedRowParallel:
     leave the arrival counters of the signal buffer partly counted, which a
     later call would misread.  `check()` (collective: every rank calls it)
     reads the status on every rank and, if any rank timed out, zeroes the
-    signal buffers everywhere, restarts the epoch and raises B2XError.
-    `reset()` does the clearing alone; it also runs, collectively, before the
-    32-bit epoch would wrap.
+    signal buffers everywhere and raises B2XError.
+    `reset()` does the clearing alone.  The calls are counted by the kernel
+    in the signal buffer (epoch 0 in the C arguments), so a call has no
+    per-call host state and can be captured in a CUDA graph.
     """
 
     def __init__(self, M: int, N: int, device, group=None, mode: str = "auto"):
@@ -129,7 +130,6 @@ class FusedRowParallel:
         self._ar = ar
         self._handles = (h_out, h_sig)
         self._plans = {}  # GEMM argument structs per (operands, config): the host cost of a repeat call is one C call
-        self.epoch = 0
         torch.cuda.synchronize(self.device)
         dist.barrier(self.group)  # every rank's signal buffer is zero before any kernel runs
 
@@ -155,10 +155,7 @@ class FusedRowParallel:
             if len(self._plans) > 64:
                 self._plans.clear()
             self._plans[key] = g
-        if self.epoch >= 0xFFFFFFFF:
-            self.reset()  # every rank reaches this call at the same count
-        self.epoch += 1
-        self._ar.epoch = self.epoch
+        self._ar.epoch = 0  # the kernel counts the calls in the signal buffer (graph-capturable)
         with torch.cuda.device(self.device):
             st = L.lib().b2x_fp8_gemm_allreduce(ctypes.byref(g), ctypes.byref(self._ar),
                                                 ctypes.c_void_p(torch.cuda.current_stream(self.device).cuda_stream))
@@ -167,14 +164,13 @@ class FusedRowParallel:
 
 
     def reset(self) -> None:
-        """Collective: zero the signal buffer on every rank and restart the
-        epoch.  No fused call may be in flight on any rank."""
+        """Collective: zero the signal buffer (counters and call count) on every
+        rank.  No fused call may be in flight on any rank."""
         torch.cuda.synchronize(self.device)
         dist.barrier(self.group)
         self.signal.zero_()
         torch.cuda.synchronize(self.device)
         dist.barrier(self.group)
-        self.epoch = 0
 
     def check(self) -> None:
         """Collective: raise B2XError (after reset()) if a fused call on any
@@ -191,29 +187,44 @@ class FusedRowParallel:
                                             f"(device status 0x{int(flag.item()):x}); signal buffers were reset")
 
 
+def _default_swiglu(x, w_gu, sx, sw, h_scale, h_amax=None):
+    from .ops import gemm_swiglu
+    h, _ = gemm_swiglu(x, w_gu, sx, sw, mode="given", h_scale=h_scale, h_amax=h_amax)
+    return h
+
+
 class LlamaFP8LinearSet:
     """The Llama-3-70B-shaped fp8 linear set of one transformer block at a
-    fixed token count, sharded over the process group: QKV and gate+up
-    column-parallel, down row-parallel + all-reduce.
+    fixed token count, chained the way the block uses it and sharded over the
+    process group:
 
-    comm = "fused" (default on GPUs): the down projection and the sum of its
-    partials over the group are one kernel (FusedRowParallel).  With
-    down_sms > 0 it runs on a side stream on that many SMs while QKV and
-    gate+up run on the rest, so its NVLink traffic overlaps all of the step's
-    compute; with down_sms = 0 the three GEMMs run one after another on all
-    SMs.
-    comm = "nccl": down first, its NCCL all-reduce issued on a side stream,
-    then QKV and gate+up on the compute stream while the all-reduce runs
-    (launched with NUM_SMS = all but `comm_sms` SMs so NCCL's kernels find
-    free SMs).
+      qkv = x . Wqkv^T                        (bf16 out; column-parallel, no collective)
+      h   = fp8(silu(x . Wg^T) * (x . Wu^T))  (gate+up GEMM with the SwiGLU and the
+                                               fp8 quantization of h in its epilogue;
+                                               column-parallel, no collective)
+      out = sum over ranks of h_r . Wd_r^T    (bf16 out; row-parallel: h's column shard
+                                               is exactly down's K shard, + all-reduce)
+
+    h is quantized with a static per-tensor scale (amax / 448 of one
+    calibration pass at construction, the static activation scaling of fp8
+    inference).  Wgu is the interleaved gate/up weight (interleave_gate_up):
+    a contiguous row shard of it yields a contiguous column shard of h.
+
+    comm = "fused" (default on GPUs): the down GEMM and the sum of its partials
+    over the group are one kernel (FusedRowParallel).  comm = "nccl": the
+    down GEMM followed by an NCCL all-reduce of its output.  The three GEMMs
+    run one after another on all SMs.
+
+    `mm` and `swiglu` are injectable so the partitioning can be checked on
+    CPU ranks against an unsharded product.
     """
 
     SHAPES = {"qkv": (8192, 10240, 8192), "gate_up": (8192, 57344, 8192), "down": (8192, 8192, 28672)}
 
-    def __init__(self, rank: int, world: int, device, tokens: int = 8192, seed: int = 1234, comm_sms: int = 16,
-                 mm: Callable = _default_mm, make_input: Optional[Callable] = None, comm: str = "fused",
-                 fused_mode: str = "auto", down_sms: Optional[int] = None):
-        self.rank, self.world, self.device, self.mm = rank, world, device, mm
+    def __init__(self, rank: int, world: int, device, tokens: int = 8192, seed: int = 1234,
+                 mm: Callable = _default_mm, swiglu: Callable = _default_swiglu, make_input: Optional[Callable] = None,
+                 comm: str = "fused", fused_mode: str = "auto"):
+        self.rank, self.world, self.device, self.mm, self.swiglu = rank, world, device, mm, swiglu
         self.tokens = tokens
         M = tokens
         K = self.SHAPES["qkv"][2]
@@ -221,12 +232,14 @@ class LlamaFP8LinearSet:
         ngu = self.SHAPES["gate_up"][1] // world
         kd = self.SHAPES["down"][2] // world
         nd = self.SHAPES["down"][1]
+        if ngu != 2 * kd or kd % 128:
+            raise ValueError("gate+up must produce down's K shard in 128-column blocks")
         make = make_input or _rand_fp8
-        g = torch.Generator(device=device).manual_seed(seed + rank)
-        self.x, self.sx = make((M, K), g, device)
+        gx = torch.Generator(device=device).manual_seed(seed)  # the activations are the same on every rank
+        self.x, self.sx = make((M, K), gx, device)
+        g = torch.Generator(device=device).manual_seed(seed + 1 + rank)
         self.wq, self.sq = make((nq, K), g, device)
         self.wgu, self.sgu = make((ngu, K), g, device)
-        self.a2, self.sa2 = make((M, kd), g, device)
         self.wd, self.sd = make((nd, kd), g, device)
         self.flops_total = sum(2.0 * (M / 8192) * m * n * k for (m, n, k) in self.SHAPES.values())
         on_gpu = world > 1 and torch.device(device).type == "cuda"
@@ -234,64 +247,57 @@ class LlamaFP8LinearSet:
             raise ValueError(f"comm must be 'fused' or 'nccl', got {comm!r}")
         self.comm = comm if on_gpu else "nccl"
         self.fused = FusedRowParallel(M, nd, device, mode=fused_mode) if self.comm == "fused" else None
-        self.comm_stream = torch.cuda.Stream(device) if on_gpu else None
-        n_sms = torch.cuda.get_device_properties(device).multi_processor_count if on_gpu else 0
-        self.overlap_cfg = {"NUM_SMS": n_sms - comm_sms} if on_gpu else {}
         self.cfg = {}
-        if self.fused is not None:
-            # SMs for the fused down kernel: its share of the step's FLOPs, in CTA pairs
-            if down_sms is None:
-                share = (self.SHAPES["down"][1] * self.SHAPES["down"][2]) / sum(
-                    n * k for (_, n, k) in self.SHAPES.values())
-                down_sms = 2 * round(share * n_sms / 2)
-            self.down_sms = int(down_sms)
-            self.down_cfg = {"NUM_SMS": self.down_sms} if self.down_sms > 0 else {}
-            self.rest_cfg = {"NUM_SMS": n_sms - self.down_sms} if self.down_sms > 0 else {}
+        self.sh = self._calibrate_h_scale()
+
+    def _calibrate_h_scale(self) -> torch.Tensor:
+        one = torch.ones(1, dtype=torch.float32, device=self.device)
+        amax = torch.zeros(1, dtype=torch.float32, device=self.device)
+        self.swiglu(self.x, self.wgu, self.sx, self.sgu, one, amax)
+        sh = amax / 448.0
+        return torch.where(sh > 0, sh, one)
+
+    def capture(self):
+        """Record step() once in a CUDA graph (collective: every rank calls it).
+        replay() then runs the three kernels with no host work per launch;
+        the fused all-reduce counts its calls on the device, so every replay
+        is a new call.  Returns the (qkv_out, h, down_out) tensors that every
+        replay overwrites."""
+        dev = torch.device(self.device)
+        s = torch.cuda.Stream(dev)
+        s.wait_stream(torch.cuda.current_stream(dev))
+        with torch.cuda.stream(s):
+            self.step()  # builds the argument plans and the allocator's blocks
+        torch.cuda.synchronize(dev)
+        if self.world > 1:
+            dist.barrier()
+        from ._lib import launch_count
+        self.graph = torch.cuda.CUDAGraph()
+        n0 = launch_count()
+        with torch.cuda.graph(self.graph, stream=s):
+            self.graph_outputs = self.step()
+        self.graph_launches = launch_count() - n0  # libb2x kernels per replay
+        torch.cuda.synchronize(dev)
+        return self.graph_outputs
+
+    def replay(self):
+        """One step by replaying the graph of capture()."""
+        self.graph.replay()
+        return self.graph_outputs
 
     def step(self, events=None):
-        """One pass over the set; returns (qkv_out, gate_up_out, down_out)."""
-        if self.fused is not None:
-            if self.down_sms == 0:
-                d = self.fused(self.a2, self.sa2, self.wd, self.sd)
-            else:
-                ready = torch.cuda.Event()
-                ready.record()
-                with torch.cuda.stream(self.comm_stream):
-                    self.comm_stream.wait_event(ready)
-                    d = self.fused(self.a2, self.sa2, self.wd, self.sd, self.down_cfg)
-            q = self.mm(self.x, self.wq, self.sx, self.sq, self.rest_cfg)
-            if events:
-                events[0].record()
-            gu = self.mm(self.x, self.wgu, self.sx, self.sgu, self.rest_cfg)
-            if events:
-                events[1].record()
-            if self.down_sms:
-                torch.cuda.current_stream().wait_stream(self.comm_stream)
-            return q, gu, d
-        if self.world > 1 and self.comm_stream is not None:
-            d = self.mm(self.a2, self.wd, self.sa2, self.sd, self.cfg)
-            ready = torch.cuda.Event()
-            ready.record()
-            with torch.cuda.stream(self.comm_stream):
-                self.comm_stream.wait_event(ready)
-                dist.all_reduce(d)
-            d.record_stream(self.comm_stream)
-            q = self.mm(self.x, self.wq, self.sx, self.sq, self.overlap_cfg)
-            if events:
-                events[0].record()
-            gu = self.mm(self.x, self.wgu, self.sx, self.sgu, self.overlap_cfg)
-            if events:
-                events[1].record()
-            torch.cuda.current_stream().wait_stream(self.comm_stream)
-            return q, gu, d
+        """One pass over the set; returns (qkv_out, h, down_out)."""
         q = self.mm(self.x, self.wq, self.sx, self.sq, self.cfg)
         if events:
             events[0].record()
-        gu = self.mm(self.x, self.wgu, self.sx, self.sgu, self.cfg)
+        h = self.swiglu(self.x, self.wgu, self.sx, self.sgu, self.sh)
         if events:
             events[1].record()
-        d = row_parallel(self.a2, self.sa2, self.wd, self.sd, mm=self.mm, cfg=self.cfg)
-        return q, gu, d
+        if self.fused is not None:
+            d = self.fused(h, self.sh, self.wd, self.sd)
+        else:
+            d = row_parallel(h, self.sh, self.wd, self.sd, mm=self.mm, cfg=self.cfg)
+        return q, h, d
 
 
 def _rand_fp8(shape, gen, device):

@@ -677,7 +677,6 @@ b2x_status b2x_fp8_gemm_allreduce(const b2x_gemm_args* args, const b2x_allreduce
   }
   if (mc && (((uintptr_t)r->c_multicast % 16) || ((uintptr_t)r->signal_multicast % 16)))
     return fail(B2X_ERR_INVALID_ARG, "b2x_fp8_gemm_allreduce: multicast addresses must be 16-byte aligned");
-  if (r->epoch == 0) return fail(B2X_ERR_INVALID_ARG, "b2x_fp8_gemm_allreduce: epoch starts at 1");
   ArParams ar;
   memset(&ar, 0, sizeof(ar));
   ar.mode = mc ? 1 : 2;
@@ -690,6 +689,8 @@ b2x_status b2x_fp8_gemm_allreduce(const b2x_gemm_args* args, const b2x_allreduce
     ar.sig_peer[i] = reinterpret_cast<uint32_t*>(r->signal_peers[i]);
   }
   const uint32_t units = (uint32_t)(b2x_allreduce_signal_words(args->M, args->N) - kArArrive0);
+  ar.units = units;
+  ar.device_epoch = r->epoch == 0;
   ar.done_target = r->epoch * units;  // wraps modulo 2^32, compared as a difference
   b2x_gemm_args a = *args;
   a.config.block_n = 256;

@@ -25,11 +25,14 @@ cudaError_t launch_amax(const void* x, b2x_dtype xt, int64_t rows, int64_t cols,
 // Fused all-reduce of the GEMM output over the GPUs of one node
 // (b2x_fp8_gemm_allreduce).  Signal buffer layout, in 32-bit words on every
 // rank: word 0 counts finished reductions (done), word 1 the units this rank
-// reduced (diagnostic), words [kArArrive0, kArArrive0 + units) count, per
+// reduced (diagnostic), word 2 (kArEpochWord) the calls completed on this rank
+// when the call count is kept on the device, words [kArArrive0, kArArrive0 +
+// units) count, per
 // 128 x 256 output unit, the ranks whose partial has landed (kept on the
 // unit's owner rank, ar_owner in fp8_gemm_allreduce.cuh).
 constexpr int kArMaxRanks = 8;
 constexpr int kArArrive0 = 64;
+constexpr int kArEpochWord = 2;
 struct ArParams {
   int mode;                        // 0 off, 1 NVSwitch multicast, 2 peer loads/stores
   int rank, world;
@@ -37,7 +40,9 @@ struct ArParams {
   uint8_t* c_peer[kArMaxRanks];    // C on every rank (mode 2)
   uint32_t* sig_peer[kArMaxRanks]; // signal buffer on every rank
   uint32_t* sig_mc;                // multicast address of the signal buffer (mode 1)
-  uint32_t done_target;            // value of the done word once this call is complete
+  uint32_t done_target;            // value of the done word once this call is complete (host-counted calls)
+  uint32_t units;                  // 128 x 256 output units of the call
+  int device_epoch;                // 1: the call count lives in word kArEpochWord and the kernel advances it
 };
 
 struct GemmLaunch {

@@ -113,10 +113,10 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volati
 //   2 MMA waiting for a free accumulator    3 epilogue WG0 waiting for data
 //   4 epilogue WG1 waiting for data         5 CTA lifetime (thread 0)
 //   6 MMA issue (data ready to commit)      7 units processed by the CTA
-// and, for the fused GEMM + all-reduce (paired kernel):
-//   8 reducing owned units                  9 waiting for peers' arrivals (queue full / drain)
-//  10 units reduced inside the tile loop   11 units reduced after it (drain)
-//  12 final wait for every rank's reductions  13 tile-loop end to drain end
+// and, for the fused GEMM + all-reduce (paired kernel; its reducer warpgroup):
+//   8 reducing owned units                  9 waiting for peers' arrivals
+//  10 units reduced                        12 final wait for every rank's reductions
+//  13 reducer lifetime up to the final wait
 constexpr int kTraceSlots = 16;
 constexpr int kTraceMaxCtas = 512;
 __device__ unsigned long long g_trace[kTraceMaxCtas * kTraceSlots];
@@ -415,6 +415,11 @@ __device__ __forceinline__ void red_add_release_sys(uint32_t* p, uint32_t v) {
 }
 __device__ __forceinline__ void st_relaxed_sys(uint32_t* p, uint32_t v) {
   asm volatile("st.relaxed.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ uint32_t ld_relaxed_sys(const uint32_t* p) {
+  uint32_t v;
+  asm volatile("ld.relaxed.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
 }
 __device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
   uint32_t v;

@@ -11,24 +11,27 @@
 //      stores to complete, publishes them at system scope and adds 1 to the
 //      unit's arrival counter, kept on the unit's owner rank (a hash of the
 //      unit index spreads the units evenly over the ranks);
-//   2. the owner's warpgroup that stored the same unit queues it; between
-//      tiles it checks (without blocking) whether the oldest queued unit has
-//      all arrivals and if so reduces it: mode 1 reads the unit once through
-//      the multicast address (multimem.ld_reduce: the switch fetches every
-//      rank's copy and adds them in fp32) and writes the bf16 sum back
-//      through the same address (multimem.st: the switch stores it on every
-//      rank); mode 2 reads every rank's copy over NVLink, adds in fp32 in
-//      rank order and stores the sum to every rank;
+//   2. if this rank owns the unit, the warpgroup also pushes it into a ring in
+//      shared memory, read by a fifth warpgroup of the CTA that does nothing
+//      but reduce: for each owned unit, in the order the epilogues stored
+//      them, it waits (bounded) until the unit has all arrivals and reduces
+//      it -- mode 1 reads the unit once through the multicast address
+//      (multimem.ld_reduce: the switch fetches every rank's copy and adds
+//      them in fp32) and writes the bf16 sum back through the same address
+//      (multimem.st: the switch stores it on every rank); mode 2 reads every
+//      rank's copy over NVLink, adds in fp32 in rank order and stores the sum
+//      to every rank;
 //   3. it resets the arrival counter and adds 1 to the done word of every rank.
-// A queue that fills up, and the queue left at the end of the tile loop, are
-// served with bounded waits.  These waits cannot form a cycle: every rank
-// launches the same grid, so a unit is stored by the same warpgroup index on
-// every rank, in the same sequence; a warpgroup waits only for a unit it has
-// already stored, i.e. for a peer's same warpgroup that is behind it in that
-// sequence, and following such waits always leads to a warpgroup that is not
-// waiting.  Each rank's kernel ends with one bounded wait
-// until its done word shows every unit of this call reduced, so the output
-// is complete on every rank when the kernel retires.
+// So the GEMM's epilogues never wait for a peer: the reductions run beside
+// the tile loop and keep NVLink busy while the tensor cores work.  The waits
+// cannot form a cycle: every rank launches the same grid, so a unit is
+// stored by the same CTA and warpgroup on every rank, in the same sequence,
+// and a reducer waits only for units its own CTA has already stored, i.e.
+// for peers' same CTA that are behind in that sequence.  A full ring makes
+// an epilogue wait for its reducer, which again waits only on such units.
+// After its last unit the reducer waits (bounded) until its done word shows
+// every unit of this call reduced, so the output is complete on every rank
+// when the kernel retires.
 //
 // The done word grows by `units` per call, so consecutive calls need no
 // clearing as long as every rank makes the same calls in the same order.
@@ -79,15 +82,15 @@ __device__ __forceinline__ void ar_reduce_unit(const GemmParams& p, int unit, in
   // 128 rows x 512 bytes = 4096 16-byte vectors; 32 consecutive threads cover one row.
   if constexpr (AR == 1) {
 #pragma unroll 1
-    for (int it = 0; it < 32; it += 8) {
-      uint4 v[8];
+    for (int it = 0; it < 32; it += 16) {
+      uint4 v[16];
 #pragma unroll
-      for (int j = 0; j < 8; ++j) {
+      for (int j = 0; j < 16; ++j) {
         const int idx = (it + j) * 128 + wg_tid;
         v[j] = multimem_ld_reduce_bf16x8(ar.c_mc + base + (idx >> 5) * rb + (idx & 31) * 16);
       }
 #pragma unroll
-      for (int j = 0; j < 8; ++j) {
+      for (int j = 0; j < 16; ++j) {
         const int idx = (it + j) * 128 + wg_tid;
         multimem_st_16(ar.c_mc + base + (idx >> 5) * rb + (idx & 31) * 16, v[j]);
       }
@@ -131,66 +134,96 @@ __device__ __forceinline__ void ar_reduce_unit(const GemmParams& p, int unit, in
   fence_acq_rel_sys();  // this thread's share of the sum is visible on every rank
 }
 
-// Per-warpgroup queue of owned units waiting for their arrivals (shared
-// memory, touched by thread 0 only) and the word that broadcasts thread 0's
-// decision to the warpgroup.
-constexpr int kArQueue = 16;
-struct ArQueue {
-  int unit[kArQueue];
-  int head, count;
-  int cmd;  // >= 0: reduce this unit; -1: nothing to do; -2: gave up (timeout)
-  int pad;
+// Ring of owned units in shared memory, from the two epilogue warpgroups
+// (producers, thread 0 of each) to the reducer warpgroup (thread 0).  A slot
+// holds unit + 1, 0 when free; producers take tickets with an atomic add and
+// wait (bounded) for their slot to be free.
+constexpr int kArRing = 32;
+struct ArRing {
+  int slot[kArRing];
+  int tail;  // tickets taken by the producers
+  int cmd;   // reducer thread 0 -> its warpgroup: unit to reduce, -1 stop
 };
 
-// One warpgroup after storing `unit` (unit < 0: end of the tile loop, drain
-// the queue).  Reduces at most `max_reduce` ready units, waiting (bounded)
-// only when the queue is full or when draining.
-template <int AR>
-__device__ __forceinline__ void ar_service(const GemmParams& p, int unit, int wg_tid, uint32_t bar_id,
-                                           volatile ArQueue* q) {
-  const ArParams& ar = p.ar;
-  const bool drain = unit < 0;
-  if (wg_tid == 0 && !drain) {
-    ar_arrive(ar, unit);
-    if (ar_owner(unit, ar.world) == ar.rank) {
-      q->unit[(q->head + q->count) % kArQueue] = unit;
-      q->count = q->count + 1;
+__device__ __forceinline__ bool ar_ring_push(volatile ArRing* r, int unit, volatile int* abort) {
+  const int t = atomicAdd(const_cast<int*>(&r->tail), 1);
+  volatile int* s = &r->slot[t % kArRing];
+  const uint64_t start = globaltimer();
+  while (*s != 0) {
+    if (*abort) return false;
+    if (globaltimer() - start > kArWaitNs) {
+      atomicCAS(&g_status, 0, kStatusTimeoutAllReduce);
+      *abort = 1;
+      return false;
     }
+    __nanosleep(64);
   }
-  for (int served = 0;; ++served) {
+  *s = unit + 1;
+  return true;
+}
+
+__device__ __forceinline__ int ar_ring_pop(volatile ArRing* r, int ticket, volatile int* abort) {
+  volatile int* s = &r->slot[ticket % kArRing];
+  const uint64_t start = globaltimer();
+  int v;
+  while ((v = *s) == 0) {
+    if (*abort) return -1;
+    if (globaltimer() - start > kArWaitNs) {
+      atomicCAS(&g_status, 0, kStatusTimeoutAllReduce);
+      *abort = 1;
+      return -1;
+    }
+    __nanosleep(32);
+  }
+  *s = 0;
+  return v - 1;
+}
+
+// Number of units the CTA at cluster rank `crank` of cluster `cluster_id`
+// stores during the tile loop that this GPU rank owns.
+__device__ __forceinline__ int ar_owned_units(const GemmParams& p, int cluster_id, int num_clusters, int crank) {
+  int n = 0;
+  for (int tile = cluster_id; tile < p.num_units; tile += num_clusters)
+    n += ar_owner(2 * tile + crank, p.ar.world) == p.ar.rank;
+  return n;
+}
+
+// The reducer warpgroup (128 threads, named barrier `bar_id`).  Returns
+// false if it gave up (a peer never arrived, or the GEMM aborted).
+template <int AR>
+__device__ __forceinline__ bool ar_reducer(const GemmParams& p, int n_owned, int wg_tid, uint32_t bar_id,
+                                           volatile ArRing* ring, volatile int* abort) {
+  const ArParams& ar = p.ar;
+  bool ok = true;
+  for (int i = 0; i < n_owned; ++i) {
     if (wg_tid == 0) {
-      int cmd = -1;
-      if (q->count > 0 && (drain || served < 2)) {
-        const int u = q->unit[q->head];
-        const uint32_t* ctr = ar.sig_peer[ar.rank] + kArArrive0 + u;
-        bool ready = ld_acquire_sys(ctr) >= (uint32_t)ar.world;
-        if (!ready && (drain || q->count == kArQueue)) {
-          const long long t0 = clock64();
-          ready = wait_counter_sys(ctr, (uint32_t)ar.world, kArWaitNs);
-          trace_add(p.trace, 9, (unsigned long long)(clock64() - t0));
-        }
-        if (ready) {
+      int cmd = ar_ring_pop(ring, i, abort);
+      if (cmd >= 0) {
+        const uint32_t* ctr = ar.sig_peer[ar.rank] + kArArrive0 + cmd;
+        const long long t0 = clock64();
+        if (ld_acquire_sys(ctr) < (uint32_t)ar.world && !wait_counter_sys(ctr, (uint32_t)ar.world, kArWaitNs)) {
+          *abort = 1;
+          cmd = -1;
+        } else {
           st_relaxed_sys(const_cast<uint32_t*>(ctr), 0u);  // all arrived: reset for the next call
-          q->head = (q->head + 1) % kArQueue;
-          q->count = q->count - 1;
-          cmd = u;
-        } else if (drain || q->count == kArQueue) {
-          cmd = -2;  // a peer never arrived; the status word says so
-          q->count = 0;
         }
+        trace_add(p.trace, 9, (unsigned long long)(clock64() - t0));
       }
-      q->cmd = cmd;
+      ring->cmd = cmd;
     }
     named_bar_sync(bar_id, 128);
-    const int cmd = q->cmd;
+    const int cmd = ring->cmd;
     named_bar_sync(bar_id, 128);  // everyone has read cmd before thread 0 rewrites it
-    if (cmd < 0) break;
+    if (cmd < 0) {
+      ok = false;
+      break;
+    }
     const long long t0 = clock64();
     ar_reduce_unit<AR>(p, cmd, wg_tid);
     named_bar_sync(bar_id, 128);
     if (wg_tid == 0) {
       trace_add(p.trace, 8, (unsigned long long)(clock64() - t0));
-      trace_add(p.trace, drain ? 11 : 10, 1);
+      trace_add(p.trace, 10, 1);
       if constexpr (AR == 1) {
         multimem_red_add_release_sys(ar.sig_mc, 1u);
       } else {
@@ -199,6 +232,7 @@ __device__ __forceinline__ void ar_service(const GemmParams& p, int unit, int wg
       atomicAdd(ar.sig_peer[ar.rank] + 1, 1u);  // units this rank reduced (diagnostic)
     }
   }
+  return ok;
 }
 
 }  // namespace b2x

@@ -50,15 +50,20 @@ struct PairSmem {
   static constexpr int kBarOff = kCOff + 2 * kCBytes;
   static constexpr int kBarBytes = (2 * STAGES + 5) * 8 + 16;
   static constexpr int kQOff = (kBarOff + kBarBytes + 15) / 16 * 16;  // fused all-reduce queues
-  static constexpr int kAlloc = kQOff + 2 * (int)sizeof(ArQueue) + 1024;
+  static constexpr int kAlloc = kQOff + (int)sizeof(ArRing) + 1024;
 };
 
 // AR: 0 plain GEMM; 1 / 2 the GEMM output is summed over the node's GPUs as
 // its units are stored (fp8_gemm_allreduce.cuh; 1 NVSwitch multicast, 2 peer
 // loads and stores).  EPI: 1 = the fused SwiGLU + fp8 quantize epilogue
 // (fp8_gemm_swiglu.cuh; tmC then maps the fp8 output h).
+template <int AR>
+constexpr int pair_threads() {
+  return AR != 0 ? kThreads + 128 : kThreads;  // + the reducer warpgroup of the fused all-reduce
+}
+
 template <int STAGES, int B_MN, int AR, int EPI = 0>
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __launch_bounds__(pair_threads<AR>(), 1)
     fp8_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                          const __grid_constant__ CUtensorMap tmC, const GemmParams p) {
   using L = PairSmem<STAGES>;
@@ -73,7 +78,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* mma_done = tempty + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(mma_done + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
-  volatile ArQueue* ar_queue = reinterpret_cast<volatile ArQueue*>(smem + L::kQOff);  // one per epilogue warpgroup
+  volatile ArRing* ar_ring = reinterpret_cast<volatile ArRing*>(smem + L::kQOff);  // owned units for the reducer
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -91,7 +96,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     mbar_init(mma_done, 1);
     *abort_flag = 0;
-    for (int i = 0; i < 2; ++i) ar_queue[i].head = ar_queue[i].count = 0;
+    for (int i = 0; i < kArRing; ++i) ar_ring->slot[i] = 0;
+    ar_ring->tail = 0;
+    ar_ring->cmd = 0;
     fence_barrier_init();
   }
   if (warp == 0 && lane == 0) {
@@ -201,7 +208,33 @@ __global__ void __launch_bounds__(kThreads, 1)
       volatile int no_abort = 0;
       mbar_wait(mma_done, 0, &no_abort, kStatusTimeoutMma);
     }
-  } else if (warp >= kEpiWarp0) {
+  } else if (AR != 0 && warp >= kEpiWarp0 + 8) {
+    // ------------------------------------------------------------ all-reduce reducer (both CTAs)
+    const int wg_tid = threadIdx.x - (kEpiWarp0 + 8) * 32;
+    const uint32_t bar_id = 3;
+    // With the call count kept on the device, this call is number count + 1.
+    // The count is read before any unit of this CTA is stored; the CTA that
+    // advances it does so only after every unit of the call (this CTA's
+    // included) has been reduced, so no CTA can read an advanced count.
+    uint32_t call_no = 0, done_target = p.ar.done_target;
+    if (p.ar.device_epoch && wg_tid == 0) {
+      call_no = ld_relaxed_sys(p.ar.sig_peer[p.ar.rank] + kArEpochWord) + 1u;
+      done_target = call_no * p.ar.units;  // modulo 2^32, like the done word
+    }
+    const int n_owned = ar_owned_units(p, cluster_id, num_clusters, (int)rank);
+    const long long t_red = clock64();
+    const bool ok = ar_reducer<AR>(p, n_owned, wg_tid, bar_id, ar_ring, abort_flag);
+    if (wg_tid == 0) trace_add(p.trace, 13, (unsigned long long)(clock64() - t_red));
+    // The output is complete here once every unit of this call has been
+    // reduced by its owner rank.
+    if (ok && wg_tid == 0 && !*abort_flag) {
+      const long long t0 = clock64();
+      const bool done = wait_counter_sys(p.ar.sig_peer[p.ar.rank], done_target, kArWaitNs);
+      trace_add(p.trace, 12, (unsigned long long)(clock64() - t0));
+      if (done && p.ar.device_epoch && blockIdx.x == 0)
+        st_relaxed_sys(p.ar.sig_peer[p.ar.rank] + kArEpochWord, call_no);
+    }
+  } else if (warp >= kEpiWarp0 && warp < kEpiWarp0 + 8) {
     // ------------------------------------------------------------ epilogue (both CTAs)
     const int e = (warp - kEpiWarp0) >> 2;
     const int q = warp & 3;
@@ -270,22 +303,17 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
         }
       }
-      if constexpr (AR != 0) ar_service<AR>(p, 2 * tile + (int)rank, wg_tid, bar_id, ar_queue + e);
-    }
-    if (wg_tid == 0) bulk_wait_group0();
-    if constexpr (AR != 0) {
-      const long long t_drain = clock64();
-      if (wg_all(*abort_flag == 0, bar_id))
-        ar_service<AR>(p, -1, wg_tid, bar_id, ar_queue + e);  // reduce the owned units still queued
-      if (wg_tid == 0) trace_add(p.trace, 13, (unsigned long long)(clock64() - t_drain));
-      // The output is complete here once every unit of this call has been
-      // reduced by its owner rank.
-      if (e == 0 && wg_tid == 0 && !*abort_flag) {
-        const long long t0 = clock64();
-        wait_counter_sys(p.ar.sig_peer[p.ar.rank], p.ar.done_target, kArWaitNs);
-        trace_add(p.trace, 12, (unsigned long long)(clock64() - t0));
+      if constexpr (AR != 0) {
+        // publish the unit's stores and count them on its owner; owned units
+        // go to this CTA's reducer warpgroup
+        if (wg_tid == 0) {
+          const int unit = 2 * tile + (int)rank;
+          ar_arrive(p.ar, unit);
+          if (ar_owner(unit, p.ar.world) == p.ar.rank) ar_ring_push(ar_ring, unit, abort_flag);
+        }
       }
     }
+    if (wg_tid == 0) bulk_wait_group0();
   }
 
   if (threadIdx.x == 0) trace_add(p.trace, 5, (unsigned long long)(clock64() - t_start));
@@ -304,7 +332,7 @@ static cudaError_t launch_pair_t(const GemmLaunch& g, const GemmParams& p, cudaS
   cudaError_t e = ensure_smem_attr(reinterpret_cast<const void*>(kern), L::kAlloc);
   if (e != cudaSuccess) return e;
   cudaLaunchConfig_t cfg = {};
-  cfg.blockDim = dim3(kThreads, 1, 1);
+  cfg.blockDim = dim3(pair_threads<AR>(), 1, 1);
   cfg.dynamicSmemBytes = L::kAlloc;
   cfg.stream = st;
   cudaLaunchAttribute attr[1];
