@@ -36,6 +36,7 @@ enum : int {
   kStatusTimeoutEpilogue = 0x103,
   kStatusTimeoutSplitK = 0x104,
   kStatusTimeoutAllReduce = 0x105,  // a peer GPU never finished its share of a fused all-reduce
+  kStatusTimeoutCast = 0x106,       // a staged cast kernel's load never completed
 };
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
@@ -172,6 +173,17 @@ __device__ __forceinline__ void tma_store_2d(const CUtensorMap* m, const void* s
                    reinterpret_cast<uint64_t>(m)),
                "r"(smem_u32(src)), "r"(x), "r"(y)
                : "memory");
+}
+
+// 1-D bulk copy global -> shared (both 16-byte aligned, bytes % 16 == 0),
+// completion counted on `bar` in bytes.  No multicast.
+__device__ __forceinline__ void bulk_load_1d(void* dst, const void* src, uint32_t bytes, uint64_t* bar,
+                                             uint64_t policy) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1], %2, [%3], %4;" ::"r"(
+          smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(src)), "r"(bytes), "r"(smem_u32(bar)), "l"(policy)
+      : "memory");
 }
 
 __device__ __forceinline__ void bulk_commit_group() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }

@@ -411,6 +411,296 @@ __global__ void __launch_bounds__(256) quant_tile128_kernel(CastGeom g, float* s
 }
 
 // ----------------------------------------------------------------------------
+// Staged streaming kernels for contiguous tensors (the common case): a
+// producer warp streams 16 KB chunks of x into a ring of shared-memory stages
+// with 1-D bulk copies (cp.async.bulk, completion counted on an mbarrier), so
+// many KB per SM are in flight without holding registers, and 8 consumer
+// warps convert each chunk from shared memory and write q with coalesced
+// stores.  Chunk c of the tensor goes to CTA c % grid, in order.
+//
+// STAGED_MODE: 0 = cast only (NONE), 1 = one scale for the tensor (TENSOR /
+// TENSOR_GIVEN), 2 = 1x128 row-block scales (rows a multiple of 128 long, so
+// every 128 consecutive elements of the flat tensor are one group), 3 = amax
+// pass of TENSOR (per-CTA NaN-ignoring max |x| into partials).
+constexpr int kStChunk = 16384;  // bytes of x per stage
+constexpr int kStStages = 4;
+constexpr int kStConsumers = 256;
+constexpr int kStThreads = kStConsumers + 32;
+constexpr int kStSmem = kStStages * kStChunk + 2 * kStStages * 8 + 16 + 128;
+
+struct StagedArgs {
+  const uint8_t* x;     // 16-byte aligned
+  uint8_t* q;           // 16-byte aligned (unused in mode 3)
+  int64_t n;            // elements; n * sizeof(T) % 16 == 0
+  int64_t nchunks;
+  int64_t groups_per_row;  // mode 2: cols / 128
+  void* scale;          // mode 2: fp32 [rows, ld_scale]; mode 1: scale[0]
+  int64_t ld_scale;
+  int tensor_mode;      // mode 1: B2X_SCALE_TENSOR (inv from partials) or B2X_SCALE_TENSOR_GIVEN
+  uint32_t* partials;   // mode 1 (TENSOR) input, mode 3 output
+  int npartials;
+};
+
+template <typename T>
+__device__ __forceinline__ void staged_unpack(uint4 raw, float* e) {
+  if constexpr (sizeof(T) == 4) {
+    e[0] = __uint_as_float(raw.x), e[1] = __uint_as_float(raw.y);
+    e[2] = __uint_as_float(raw.z), e[3] = __uint_as_float(raw.w);
+  } else {
+    e[0] = bf16lo(raw.x), e[1] = bf16hi(raw.x), e[2] = bf16lo(raw.y), e[3] = bf16hi(raw.y);
+    e[4] = bf16lo(raw.z), e[5] = bf16hi(raw.z), e[6] = bf16lo(raw.w), e[7] = bf16hi(raw.w);
+  }
+}
+
+template <int FP8, int MODE, int VE>
+__device__ __forceinline__ void staged_store(uint8_t* qp, const float* e, float inv) {
+  if constexpr (VE == 4) {
+    const uint32_t w = MODE == 0 ? quant4<FP8, false>(make_float4(e[0], e[1], e[2], e[3]), 1.f)
+                                 : quant4<FP8>(make_float4(e[0], e[1], e[2], e[3]), inv);
+    __stcs(reinterpret_cast<unsigned int*>(qp), w);
+  } else {
+    const float(&e8)[8] = *reinterpret_cast<const float(*)[8]>(e);
+    const uint2 w = MODE == 0 ? quant8<FP8, false>(e8, 1.f) : quant8<FP8>(e8, inv);
+    __stcs(reinterpret_cast<uint2*>(qp), w);
+  }
+}
+
+template <typename T, int FP8, int MODE, bool FULL>
+__device__ __forceinline__ void staged_quant(const StagedArgs& a, const float (&e)[kStChunk / 16 / kStConsumers][16 / sizeof(T)],
+                                             int64_t off, int nvec, float inv, int lane);
+
+// One consumer warp's share of a staged chunk: vectors j * 256 + tid for
+// j < VPT (a warp reads 32 consecutive 16-byte vectors per j).  FULL: the
+// chunk holds kStChunk bytes (no bounds checks).
+template <typename T, int FP8, int MODE, bool FULL>
+__device__ __forceinline__ void staged_chunk(const StagedArgs& a, const uint8_t* buf, int64_t off, int nvec, float inv,
+                                             float& m, int lane) {
+  constexpr int VE = 16 / sizeof(T);
+  constexpr int VPT = kStChunk / 16 / kStConsumers;
+  float e[VPT][VE];
+#pragma unroll
+  for (int j = 0; j < VPT; ++j) {
+    const int v = j * kStConsumers + threadIdx.x;
+    if (FULL || v < nvec) {
+      staged_unpack<T>(*reinterpret_cast<const uint4*>(buf + v * 16), e[j]);
+    } else {
+#pragma unroll
+      for (int i = 0; i < VE; ++i) e[j][i] = 0.f;
+    }
+  }
+  if constexpr (MODE == 3) {
+#pragma unroll
+    for (int j = 0; j < VPT; ++j)
+#pragma unroll
+      for (int i = 0; i < VE; i += 2) m = fmaxf(m, fmaxf(0.f, fabsf(absmax_xs(e[j][i], e[j][i + 1]))));
+  } else {
+    staged_quant<T, FP8, MODE, FULL>(a, e, off, nvec, inv, lane);
+  }
+}
+
+template <typename T, int FP8, int MODE, bool FULL>
+__device__ __forceinline__ void staged_quant(const StagedArgs& a, const float (&e)[kStChunk / 16 / kStConsumers][16 / sizeof(T)],
+                                             int64_t off, int nvec, float inv, int lane) {
+  constexpr float FM = Fp8Traits<FP8>::kMax;
+  constexpr int VE = 16 / sizeof(T);
+  constexpr int VPT = kStChunk / 16 / kStConsumers;
+  float vinv[VPT];
+#pragma unroll
+  for (int j = 0; j < VPT; ++j) vinv[j] = inv;
+  if constexpr (MODE == 2) {
+    // A 128-element group is LPG consecutive vectors, so a warp covers GPJ
+    // groups per j.  The group maxima are reduced within each group's lanes,
+    // gathered one group per lane (group j * GPJ + h on lane j * GPJ + h), the
+    // two IEEE divisions run once for all of the warp's groups, and the
+    // inverses go back to the groups' lanes.
+    constexpr int LPG = 128 / VE;
+    constexpr int GPJ = 32 / LPG;
+    float mine = 0.f;
+#pragma unroll
+    for (int j = 0; j < VPT; ++j) {
+      float gm = 0.f;
+#pragma unroll
+      for (int i = 0; i < VE; i += 2) gm = fmaxf(gm, fabsf(absmax_xs(e[j][i], e[j][i + 1])));
+#pragma unroll
+      for (int o = LPG / 2; o; o >>= 1) gm = fmaxf(gm, __shfl_xor_sync(0xffffffffu, gm, o));
+      const float got = __shfl_sync(0xffffffffu, gm, (lane % GPJ) * LPG);
+      if (lane / GPJ == j) mine = got;
+    }
+    const float sc = __fdiv_rn(mine, FM);
+    const float minv = sc == 0.f ? 0.f : __fdiv_rn(1.0f, sc);
+    const int warp_in_cta = threadIdx.x >> 5;
+    if (lane < VPT * GPJ) {
+      // group of (j, h) = lane: its first vector is j * 256 + warp * 32 + h * LPG
+      const int jj = lane / GPJ, h = lane % GPJ;
+      const int v0 = jj * kStConsumers + warp_in_cta * 32 + h * LPG;
+      if (FULL || v0 < nvec) {
+        const int64_t grp = (off / (int64_t)sizeof(T) + (int64_t)v0 * VE) >> 7;
+        int64_t idx = grp;  // contiguous scales: the group index is the scale index
+        if (a.ld_scale != a.groups_per_row) {
+          const int64_t row = grp / a.groups_per_row;
+          idx = row * a.ld_scale + (grp - row * a.groups_per_row);
+        }
+        reinterpret_cast<float*>(a.scale)[idx] = sc;
+      }
+    }
+#pragma unroll
+    for (int j = 0; j < VPT; ++j) vinv[j] = __shfl_sync(0xffffffffu, minv, j * GPJ + lane / LPG);
+  }
+#pragma unroll
+  for (int j = 0; j < VPT; ++j) {
+    const int v = j * kStConsumers + threadIdx.x;
+    if (FULL || v < nvec) staged_store<FP8, MODE, VE>(a.q + off / (int64_t)sizeof(T) + (int64_t)v * VE, e[j], vinv[j]);
+  }
+}
+
+template <typename T, int FP8, int MODE>
+__global__ void __launch_bounds__(kStThreads, 1) cast_staged_kernel(const StagedArgs a) {
+  constexpr float FM = Fp8Traits<FP8>::kMax;
+  constexpr int VPC = kStChunk / 16;                 // vectors per chunk
+  extern __shared__ uint8_t st_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(st_raw) + 127) & ~uintptr_t(127));
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + kStStages * kStChunk);
+  uint64_t* empty = full + kStStages;
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(empty + kStStages);
+  __shared__ float s_inv;
+  __shared__ float s_red[kStThreads / 32];
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < kStStages; ++i) {
+      mbar_init(&full[i], 1);
+      mbar_init(&empty[i], kStConsumers / 32);
+    }
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  if constexpr (MODE == 1) {
+    if (a.tensor_mode == B2X_SCALE_TENSOR) {
+      const float amax = reduce_partials(a.partials, a.npartials);
+      if (threadIdx.x == 0) {
+        const float sc = __fdiv_rn(amax, FM);
+        s_inv = sc == 0.f ? 0.f : __fdiv_rn(1.0f, sc);
+        if (blockIdx.x == 0) *reinterpret_cast<float*>(a.scale) = sc;
+      }
+    } else if (threadIdx.x == 0) {
+      const float sc = *reinterpret_cast<const float*>(a.scale);
+      s_inv = sc == 0.f ? 0.f : __fdiv_rn(1.0f, sc);
+    }
+  }
+  __syncthreads();
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t bytes_total = a.n * (int64_t)sizeof(T);
+
+  if (warp == kStConsumers / 32) {
+    // ------------------------------------------------------------ producer
+    if (lane == 0) {
+      const uint64_t pol = policy_evict_first();
+      int stage = 0;
+      uint32_t phase = 0;
+      for (int64_t c = blockIdx.x; c < a.nchunks; c += gridDim.x) {
+        if (!mbar_wait(&empty[stage], phase ^ 1, abort_flag, kStatusTimeoutCast)) break;
+        const int64_t off = c * kStChunk;
+        const uint32_t bytes = (uint32_t)min((int64_t)kStChunk, bytes_total - off);
+        mbar_arrive_expect_tx(&full[stage], bytes);
+        bulk_load_1d(smem + stage * kStChunk, a.x + off, bytes, &full[stage], pol);
+        if (++stage == kStStages) stage = 0, phase ^= 1;
+      }
+    }
+    return;  // nothing below waits for the producer warp
+  }
+
+  // -------------------------------------------------------------- consumers
+  float inv = 1.0f;
+  if constexpr (MODE == 1) inv = s_inv;
+  float m = 0.f;  // mode 3
+  int stage = 0;
+  uint32_t phase = 0;
+  for (int64_t c = blockIdx.x; c < a.nchunks; c += gridDim.x) {
+    if (!mbar_wait(&full[stage], phase, abort_flag, kStatusTimeoutCast)) break;
+    const int64_t off = c * kStChunk;
+    const int nvec = (int)(min((int64_t)kStChunk, bytes_total - off) / 16);
+    const uint8_t* buf = smem + stage * kStChunk;
+    if (nvec == VPC)
+      staged_chunk<T, FP8, MODE, true>(a, buf, off, nvec, inv, m, lane);
+    else
+      staged_chunk<T, FP8, MODE, false>(a, buf, off, nvec, inv, m, lane);
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&empty[stage]);
+    if (++stage == kStStages) stage = 0, phase ^= 1;
+  }
+  if constexpr (MODE == 3) {
+#pragma unroll
+    for (int o = 16; o; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+    if (lane == 0) s_red[warp] = m;
+    named_bar_sync(1, kStConsumers);
+    if (threadIdx.x == 0) {
+      float t = 0.f;
+      for (int i = 0; i < kStConsumers / 32; ++i) t = fmaxf(t, s_red[i]);
+      a.partials[blockIdx.x] = __float_as_uint(t);
+    }
+  }
+}
+
+// Staged path eligibility: contiguous flat tensor, 16-byte aligned x and q,
+// whole 16-byte vectors; 1x128 also needs rows that are a multiple of 128.
+static bool staged_ok(const b2x_cast_args& a) {
+  const int es = a.x_type == B2X_F32 ? 4 : 2;
+  if (a.ld_x != a.cols || a.ld_q != a.cols) return false;
+  if (((uintptr_t)a.x % 16) || ((uintptr_t)a.q % 16)) return false;
+  const int64_t n = a.rows * a.cols;
+  if ((n * es) % 16 || n == 0) return false;
+  if (a.mode == B2X_SCALE_BLOCK_1x128) return a.cols % 128 == 0;
+  return a.mode == B2X_SCALE_NONE || a.mode == B2X_SCALE_TENSOR || a.mode == B2X_SCALE_TENSOR_GIVEN;
+}
+
+template <typename T, int FP8, int MODE>
+static cudaError_t launch_staged_t(const StagedArgs& sa, int num_sms, cudaStream_t st, int* grid_out = nullptr) {
+  auto k = cast_staged_kernel<T, FP8, MODE>;
+  static int per_sm = 0;  // one cache per instantiation
+  if (per_sm == 0) {
+    cudaError_t e = cudaFuncSetAttribute(reinterpret_cast<const void*>(k), cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         kStSmem);
+    if (e != cudaSuccess) return e;
+    int v = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&v, k, kStThreads, kStSmem) != cudaSuccess || v <= 0) v = 1;
+    per_sm = v;
+  }
+  int64_t grid = (int64_t)num_sms * per_sm;
+  if (grid > sa.nchunks) grid = sa.nchunks;
+  if (grid < 1) grid = 1;
+  if (grid_out) *grid_out = (int)grid;
+  k<<<(int)grid, kStThreads, kStSmem, st>>>(sa);
+  note_launch(1);
+  return cudaGetLastError();
+}
+
+template <typename T, int FP8>
+static cudaError_t launch_cast_staged(const b2x_cast_args& a, uint32_t* partials, int num_sms, cudaStream_t st) {
+  StagedArgs sa{};
+  sa.x = reinterpret_cast<const uint8_t*>(a.x);
+  sa.q = reinterpret_cast<uint8_t*>(a.q);
+  sa.n = a.rows * a.cols;
+  sa.nchunks = (sa.n * (int64_t)sizeof(T) + kStChunk - 1) / kStChunk;
+  sa.groups_per_row = a.cols / 128;
+  sa.scale = a.scale;
+  sa.ld_scale = a.ld_scale;
+  sa.tensor_mode = a.mode;
+  sa.partials = partials;
+  switch (a.mode) {
+    case B2X_SCALE_NONE: return launch_staged_t<T, FP8, 0>(sa, num_sms, st);
+    case B2X_SCALE_TENSOR_GIVEN: return launch_staged_t<T, FP8, 1>(sa, num_sms, st);
+    case B2X_SCALE_TENSOR: {
+      int np = 0;
+      cudaError_t e = launch_staged_t<T, FP8, 3>(sa, num_sms, st, &np);
+      if (e != cudaSuccess) return e;
+      sa.npartials = np;
+      return launch_staged_t<T, FP8, 1>(sa, num_sms, st);
+    }
+    case B2X_SCALE_BLOCK_1x128: return launch_staged_t<T, FP8, 2>(sa, num_sms, st);
+    default: return cudaErrorInvalidValue;
+  }
+}
+
+// ----------------------------------------------------------------------------
 // Host-side launchers (called from b2x_api.cu after argument validation).
 
 // CTAs of 256 threads that fit on one SM at once (per kernel, cached).
@@ -434,9 +724,11 @@ static int grid_for(int64_t nsegs, int segs_per_warp, int per_sm, int num_sms) {
   return (int)blocks;
 }
 
-// Upper bound on the per-tensor amax partials (one per CTA of the amax pass).
+// Upper bound on the per-tensor amax partials (one per CTA of the amax pass,
+// whichever kernel runs it: at most 8 resident CTAs per SM in either).
 int cast_num_partials(int64_t nsegs, int num_sms) {
-  return grid_for(nsegs, 4, 8, num_sms);
+  (void)nsegs;
+  return 8 * num_sms;
 }
 
 template <typename T, int FP8>
@@ -516,6 +808,15 @@ static CastGeom make_geom(const void* x, b2x_dtype xt, int64_t rows, int64_t col
 }
 
 cudaError_t launch_cast(const b2x_cast_args& a, int num_sms, cudaStream_t st) {
+  if (staged_ok(a)) {
+    uint32_t* partials = reinterpret_cast<uint32_t*>(a.workspace);
+    const int fp8 = a.q_type == B2X_E4M3 ? 0 : 1;
+    if (a.x_type == B2X_F32)
+      return fp8 == 0 ? launch_cast_staged<float, 0>(a, partials, num_sms, st)
+                      : launch_cast_staged<float, 1>(a, partials, num_sms, st);
+    return fp8 == 0 ? launch_cast_staged<uint16_t, 0>(a, partials, num_sms, st)
+                    : launch_cast_staged<uint16_t, 1>(a, partials, num_sms, st);
+  }
   const bool uniform = a.mode == B2X_SCALE_NONE || a.mode == B2X_SCALE_TENSOR || a.mode == B2X_SCALE_TENSOR_GIVEN;
   CastGeom g = make_geom(a.x, a.x_type, a.rows, a.cols, a.ld_x, a.q, a.ld_q, uniform);
   uint32_t* partials = reinterpret_cast<uint32_t*>(a.workspace);

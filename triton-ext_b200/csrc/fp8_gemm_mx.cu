@@ -115,17 +115,6 @@ __device__ __forceinline__ void mma_mxf8f6f4(uint32_t d_tmem, uint64_t a_desc, u
       : "memory");
 }
 
-// 1-D bulk copy global -> shared, completion counted on `bar` in bytes
-// (16-byte aligned addresses, size a multiple of 16).
-__device__ __forceinline__ void bulk_load_1d(void* dst, const void* src, uint32_t bytes, uint64_t* bar,
-                                             uint64_t policy) {
-  asm volatile(
-      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1], %2, [%3], %4;" ::"r"(
-          smem_u32(dst)),
-      "l"(src), "r"(bytes), "r"(smem_u32(bar)), "l"(policy)
-      : "memory");
-}
-
 // Row-major E8M0 scales [rows, K/32] -> tiled atoms.  One thread per output
 // word (the 4 scales of one row for one 128-deep K block); rows past `rows`
 // get zero bytes (their operand rows are zero-filled by TMA).  Grid-stride
