@@ -361,6 +361,24 @@ B2X_API const char* b2x_last_error(void);
 /* Reads and clears the device status word of the current device (blocking). */
 B2X_API b2x_status b2x_read_device_status(int* status_out);
 /*
+ * Reads and clears the device status word (blocking) and returns
+ * B2X_ERR_TIMEOUT, with a message naming the role whose wait gave up, when
+ * a kernel abandoned a bounded wait since the last read; B2X_OK otherwise.
+ * No counterpart in the reference (whose Triton kernels have no bounded
+ * waits).
+ */
+B2X_API b2x_status b2x_check_device(void);
+/*
+ * Test hook for the bounded-wait failure path (current device; off by
+ * default).  what = 1: the next paired-CTA GEMMs have their MMA warp withhold
+ * the accumulator-ready signal of its first tile, so the epilogue's wait runs
+ * out; the kernel records 0x103 in the status word and returns early, with no
+ * fault or trap.  what = 0: normal operation.  wait_timeout_ns sets the limit
+ * of every bounded mbarrier wait (0 = the default 2 s).  A test restores
+ * (0, 0) when done.  No counterpart in the reference.
+ */
+B2X_API b2x_status b2x_debug_inject(int what, uint64_t wait_timeout_ns);
+/*
  * Wait-cycle trace of the last GEMM launches (diagnostics).  When the
  * environment variable B2X_TRACE=1 is set at the first GEMM call, every GEMM
  * kernel adds, per CTA, clock cycles and counts into 16 counters: [0]

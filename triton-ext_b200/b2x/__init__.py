@@ -13,10 +13,10 @@ Every op runs in libb2x.so (hand-written CUDA for sm_100a) through its C ABI
 (include/b2x.h); there is no CPU fallback.
 """
 from . import _lib
-from ._lib import B2XError, build, launch_count, read_device_status
+from ._lib import B2XError, build, check_device, launch_count, read_device_status
 from .ops import amax, quantize, gemm_config, stoch_round, grouped_gemm, gemm_swiglu, interleave_gate_up
 from .blackwell_gemm_ws import matmul, reduce_k, get_heuristic_config
 from . import blackwell_gemm_ws, mxfp8_utils
 
 __all__ = ["matmul", "quantize", "reduce_k", "amax", "get_heuristic_config", "gemm_config", "stoch_round", "grouped_gemm", "gemm_swiglu", "interleave_gate_up",
-           "blackwell_gemm_ws", "mxfp8_utils", "B2XError", "build", "launch_count", "read_device_status"]
+           "blackwell_gemm_ws", "mxfp8_utils", "B2XError", "build", "check_device", "launch_count", "read_device_status"]

@@ -25,7 +25,7 @@ SCALE_NONE, SCALE_TENSOR, SCALE_TENSOR_GIVEN, SCALE_BLOCK_1x128, SCALE_BLOCK_128
 EXPORTED = (
     "b2x_cast_workspace_size", "b2x_fp8_cast", "b2x_amax", "b2x_gemm_default_config",
     "b2x_gemm_workspace_size", "b2x_fp8_gemm", "b2x_splitk_reduce", "b2x_last_error",
-    "b2x_read_device_status", "b2x_abi_version", "b2x_launch_count", "b2x_fp8_gemm_splitk_noalloc",
+    "b2x_read_device_status", "b2x_check_device", "b2x_debug_inject", "b2x_abi_version", "b2x_launch_count", "b2x_fp8_gemm_splitk_noalloc",
     "b2x_trace_read", "b2x_allreduce_signal_words", "b2x_fp8_gemm_allreduce",
     "b2x_stoch_round", "b2x_stoch_round_rs", "b2x_grouped_gemm_workspace_size", "b2x_fp8_grouped_gemm", "b2x_fp8_gemm_swiglu",
 )
@@ -155,6 +155,10 @@ def lib() -> ctypes.CDLL:
         L.b2x_splitk_reduce.restype = ctypes.c_int
         L.b2x_last_error.argtypes = []
         L.b2x_last_error.restype = ctypes.c_char_p
+        L.b2x_check_device.argtypes = []
+        L.b2x_check_device.restype = ctypes.c_int
+        L.b2x_debug_inject.argtypes = [ctypes.c_int, ctypes.c_uint64]
+        L.b2x_debug_inject.restype = ctypes.c_int
         L.b2x_read_device_status.argtypes = [ctypes.POINTER(ctypes.c_int)]
         L.b2x_read_device_status.restype = ctypes.c_int
         L.b2x_abi_version.argtypes = []
@@ -188,6 +192,17 @@ def read_trace(max_ctas: int = 148):
 # gave up a bounded wait: state that such a kernel may have left half-updated
 # (the cached split-K workspaces, for one) registers a hook to drop it.
 _status_hooks: list = []
+
+
+def check_device() -> None:
+    """Raises B2XError(ERR_TIMEOUT) if a kernel gave up a bounded wait since
+    the last read of the device status word (blocking; clears the word)."""
+    v = ctypes.c_int(0)
+    check(lib().b2x_read_device_status(ctypes.byref(v)))
+    if v.value:
+        for hook in list(_status_hooks):
+            hook(v.value)
+        raise B2XError(ERR_TIMEOUT, f"a kernel gave up a bounded wait (device status 0x{v.value:x})")
 
 
 def read_device_status() -> int:

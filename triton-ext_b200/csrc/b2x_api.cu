@@ -128,6 +128,34 @@ const char* b2x_last_error(void) { return t_err; }
 int b2x_abi_version(void) { return B2X_ABI_VERSION; }
 uint64_t b2x_launch_count(void) { return g_launches.load(); }
 
+b2x_status b2x_check_device(void) {
+  t_err[0] = 0;
+  int v = 0;
+  b2x_status st = b2x_read_device_status(&v);
+  if (st != B2X_OK) return st;
+  if (v != 0)
+    return fail(B2X_ERR_TIMEOUT, "a kernel gave up a bounded wait (device status 0x%x: %s)", v,
+                v == kStatusTimeoutProducer   ? "TMA producer"
+                : v == kStatusTimeoutMma      ? "MMA issuer"
+                : v == kStatusTimeoutEpilogue ? "epilogue"
+                : v == kStatusTimeoutSplitK   ? "split-K finisher"
+                : v == kStatusTimeoutAllReduce ? "fused all-reduce peer"
+                : v == kStatusTimeoutCast     ? "cast loader"
+                                              : "unknown");
+  return B2X_OK;
+}
+
+b2x_status b2x_debug_inject(int what, uint64_t wait_timeout_ns) {
+  t_err[0] = 0;
+  if (what < 0 || what > 1) return fail(B2X_ERR_INVALID_ARG, "b2x_debug_inject: what must be 0 or 1 (got %d)", what);
+  unsigned long long ns = wait_timeout_ns ? (unsigned long long)wait_timeout_ns : B2X_WAIT_TIMEOUT_NS;
+  cudaError_t e = cudaMemcpyToSymbol(g_inject, &what, sizeof(int));
+  if (e != cudaSuccess) return cuda_fail(e, "b2x_debug_inject");
+  e = cudaMemcpyToSymbol(g_wait_ns, &ns, sizeof(ns));
+  if (e != cudaSuccess) return cuda_fail(e, "b2x_debug_inject");
+  return B2X_OK;
+}
+
 b2x_status b2x_read_device_status(int* status_out) {
   int v = 0, zero = 0;
   cudaError_t e = cudaMemcpyFromSymbol(&v, g_status, sizeof(int));

@@ -29,6 +29,13 @@ namespace b2x {
 // (libb2x is built as a single translation unit, so this header is the definition.)
 __device__ int g_status = 0;
 
+// Wait limit of mbar_wait in ns (B2X_WAIT_TIMEOUT_NS unless a test lowers it
+// through b2x_debug_inject), and the test-only fault switch: 1 = the paired
+// GEMM's MMA warp withholds the accumulator-ready commit of its first tile, so
+// the epilogue's bounded wait runs out (no fault, no trap: the kernel unwinds).
+__device__ unsigned long long g_wait_ns = B2X_WAIT_TIMEOUT_NS;
+__device__ int g_inject = 0;
+
 enum : int {
   kStatusOk = 0,
   kStatusTimeoutProducer = 0x101,
@@ -98,7 +105,7 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volati
     if (mbar_try_wait(bar, parity)) return true;
     if ((it & 63u) == 0) {
       if (*abort) return false;
-      if (globaltimer() - start > B2X_WAIT_TIMEOUT_NS) {
+      if (globaltimer() - start > g_wait_ns) {
         *abort = 1;
         atomicCAS(&g_status, 0, code);
         return false;
@@ -139,6 +146,19 @@ __device__ __forceinline__ bool mbar_wait_traced(uint64_t* bar, uint32_t parity,
 // Named barrier among `count` threads (multiple of 32).
 __device__ __forceinline__ void named_bar_sync(uint32_t id, uint32_t count) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");
+}
+
+// Two independent fp32 FMAs in one instruction (sm_100 paired FP32):
+// a0 = fma(x0, s, a0), a1 = fma(x1, s, a1), each rounded like fmaf.
+__device__ __forceinline__ void fma2_scalar(float& a0, float& a1, float x0, float x1, float s) {
+  asm("{\n\t.reg .b64 ra, rx, rs;\n\t"
+      "mov.b64 ra, {%0, %1};\n\t"
+      "mov.b64 rx, {%2, %3};\n\t"
+      "mov.b64 rs, {%4, %4};\n\t"
+      "fma.rn.f32x2 ra, rx, rs, ra;\n\t"
+      "mov.b64 {%0, %1}, ra;\n\t}"
+      : "+f"(a0), "+f"(a1)
+      : "f"(x0), "f"(x1), "f"(s));
 }
 
 // ---------------------------------------------------------------- TMA
@@ -275,6 +295,15 @@ __device__ __forceinline__ void tmem_ld_32x32b_x16(uint32_t taddr, uint32_t (&r)
       : "r"(taddr));
 }
 __device__ __forceinline__ void tmem_ld_wait() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+// Orders later uses of r after the preceding tmem_ld_wait(): the registers
+// pass through an empty volatile asm, so no read of them can be scheduled
+// before the wait (used where several loads are in flight).
+__device__ __forceinline__ void tmem_regs_after_wait(uint32_t (&r)[16]) {
+  asm volatile(""
+               : "+r"(r[0]), "+r"(r[1]), "+r"(r[2]), "+r"(r[3]), "+r"(r[4]), "+r"(r[5]), "+r"(r[6]), "+r"(r[7]),
+                 "+r"(r[8]), "+r"(r[9]), "+r"(r[10]), "+r"(r[11]), "+r"(r[12]), "+r"(r[13]), "+r"(r[14]),
+                 "+r"(r[15]));
+}
 
 // Shared-memory matrix descriptor (sm_100 "version 1" format) for a tile stored
 // in the canonical 128-byte-swizzled layout: rows of 128 bytes, 8-row atoms of

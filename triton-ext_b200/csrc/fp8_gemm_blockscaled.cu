@@ -213,11 +213,13 @@ __global__ void __launch_bounds__(kThreads, 1)
         tmem_ld_32x32b_x32(t, v);
         tmem_ld_wait();
 #pragma unroll
-        for (int i = 0; i < 32; ++i) acc[i] = fmaf(__uint_as_float(v[i]), s, acc[i]);
+        for (int i = 0; i < 32; i += 2)
+          fma2_scalar(acc[i], acc[i + 1], __uint_as_float(v[i]), __uint_as_float(v[i + 1]), s);
         tmem_ld_32x32b_x32(t + 32, v);
         tmem_ld_wait();
 #pragma unroll
-        for (int i = 0; i < 32; ++i) acc[32 + i] = fmaf(__uint_as_float(v[i]), s, acc[32 + i]);
+        for (int i = 0; i < 32; i += 2)
+          fma2_scalar(acc[32 + i], acc[32 + i + 1], __uint_as_float(v[i]), __uint_as_float(v[i + 1]), s);
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(&pempty[slot]);

@@ -233,20 +233,55 @@ __global__ void __launch_bounds__(BpShape<BN>::kThreads, 1)
         }
         tc_fence_after();
         const uint32_t t = tmem_base + slot * kBpBN + e * 64 + ((uint32_t)(q * 32) << 16);
-#pragma unroll
-        for (int c = 0; c < 64; c += kLC) {
-          uint32_t v[kLC];
-          if constexpr (kLC == 32)
-            tmem_ld_32x32b_x32(t + c, v);
-          else
-            tmem_ld_32x32b_x16(t + c, v);
+        if constexpr (kLC == 16) {
+          // Two-deep: the load of the next 16 columns is in flight while the
+          // FMAs of the current 16 run (tcgen05.wait::ld waits for all of a
+          // thread's loads, so each wait covers exactly one load here).
+          uint32_t v0[16], v1[16];
+          tmem_ld_32x32b_x16(t, v0);
           tmem_ld_wait();
+          tmem_regs_after_wait(v0);
 #pragma unroll
-          for (int i = 0; i < kLC; ++i) acc[c + i] = fmaf(__uint_as_float(v[i]), s, acc[c + i]);
+          for (int c = 0; c < 64; c += 32) {
+            tmem_ld_32x32b_x16(t + c + 16, v1);
+#pragma unroll
+            for (int i = 0; i < 16; i += 2)
+              fma2_scalar(acc[c + i], acc[c + i + 1], __uint_as_float(v0[i]), __uint_as_float(v0[i + 1]), s);
+            tmem_ld_wait();
+            tmem_regs_after_wait(v1);
+            if (c + 32 < 64) tmem_ld_32x32b_x16(t + c + 32, v0);
+            if (c + 32 == 64) {
+              // the whole partial is in registers: hand the slot back to the
+              // MMA warp before the last FMAs
+              tc_fence_before();
+              __syncwarp();
+              if (lane == 0) mbar_arrive_cluster_relaxed(mapa_shared(smem_u32(&pempty[slot]), 0));
+            }
+#pragma unroll
+            for (int i = 0; i < 16; i += 2)
+              fma2_scalar(acc[c + 16 + i], acc[c + 16 + i + 1], __uint_as_float(v1[i]), __uint_as_float(v1[i + 1]),
+                          s);
+            if (c + 32 < 64) {
+              tmem_ld_wait();
+              tmem_regs_after_wait(v0);
+            }
+          }
+        } else {
+#pragma unroll
+          for (int c = 0; c < 64; c += kLC) {
+            uint32_t v[kLC];
+            tmem_ld_32x32b_x32(t + c, v);
+            tmem_ld_wait();
+            if (c + kLC == 64) {
+              tc_fence_before();
+              __syncwarp();
+              if (lane == 0) mbar_arrive_cluster_relaxed(mapa_shared(smem_u32(&pempty[slot]), 0));
+            }
+#pragma unroll
+            for (int i = 0; i < kLC; i += 2)
+              fma2_scalar(acc[c + i], acc[c + i + 1], __uint_as_float(v[i]), __uint_as_float(v[i + 1]), s);
+          }
         }
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive_cluster_relaxed(mapa_shared(smem_u32(&pempty[slot]), 0));
       }
       if (!wg_all(ok, bar_id)) break;
       uint32_t pk[32];

@@ -171,6 +171,7 @@ __global__ void __launch_bounds__(pair_threads<AR>(), 1)
       uint32_t phase = 0;
       int local = 0;
       bool ok = true;
+      const bool withhold_first = g_inject == 1;  // test hook (b2x_debug_inject)
       for (int tile = cluster_id; tile < p.num_units && ok; tile += num_clusters, ++local) {
         const int buf = local & 1;
         const uint32_t use = (uint32_t)(local >> 1);
@@ -202,7 +203,7 @@ __global__ void __launch_bounds__(pair_threads<AR>(), 1)
           }
         }
         if (!ok) break;
-        mma_commit_pair_mc(&tfull[buf], 0x3);
+        if (!(withhold_first && local == 0)) mma_commit_pair_mc(&tfull[buf], 0x3);
       }
       mma_commit_pair_mc(mma_done, 0x1);
       volatile int no_abort = 0;
