@@ -238,6 +238,20 @@ B2X_API b2x_status b2x_splitk_reduce(const void* ws, b2x_dtype ws_type, void* c,
                              int64_t ldc, int split_k, void* stream);
 
 /*
+ * Same GEMM as b2x_fp8_gemm (per-tensor or no scales, split-K included) on
+ * single-CTA 128 x BLOCK_SIZE_N tiles, scheduled by cluster launch control
+ * instead of a persistent grid: the grid has one CTA per output tile (per
+ * split), each CTA starts with its own tile and then takes over the tiles of
+ * CTAs that have not launched yet (clusterlaunchcontrol.try_cancel), so work
+ * moves to the SMs that are free -- the reference's
+ * matmul_kernel_tma_ws_blackwell_clc with its host matmul
+ * (extensions/utlx/tlx/tutorials/blackwell_gemm_clc.py:62-281, :281; CLC
+ * primitives tlx/language/tlx/dynamic_launch.py:35-96).  Block / MX scales
+ * give B2X_ERR_UNSUPPORTED.
+ */
+B2X_API b2x_status b2x_fp8_gemm_clc(const b2x_gemm_args* args, void* stream);
+
+/*
  * Same GEMM as b2x_fp8_gemm, for callers that cannot allocate device memory
  * (a serving loop that reserves all memory up front, a plugin running inside
  * another framework's memory pool, a host with no allocator behind its C

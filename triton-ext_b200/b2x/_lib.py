@@ -24,7 +24,7 @@ SCALE_NONE, SCALE_TENSOR, SCALE_TENSOR_GIVEN, SCALE_BLOCK_1x128, SCALE_BLOCK_128
 
 EXPORTED = (
     "b2x_cast_workspace_size", "b2x_fp8_cast", "b2x_amax", "b2x_gemm_default_config",
-    "b2x_gemm_workspace_size", "b2x_fp8_gemm", "b2x_splitk_reduce", "b2x_last_error",
+    "b2x_gemm_workspace_size", "b2x_fp8_gemm", "b2x_fp8_gemm_clc", "b2x_splitk_reduce", "b2x_last_error",
     "b2x_read_device_status", "b2x_check_device", "b2x_debug_inject", "b2x_abi_version", "b2x_launch_count", "b2x_fp8_gemm_splitk_noalloc",
     "b2x_trace_read", "b2x_allreduce_signal_words", "b2x_fp8_gemm_allreduce",
     "b2x_stoch_round", "b2x_stoch_round_rs", "b2x_grouped_gemm_workspace_size", "b2x_fp8_grouped_gemm", "b2x_fp8_gemm_swiglu",
@@ -126,6 +126,8 @@ def lib() -> ctypes.CDLL:
         L.b2x_gemm_workspace_size.restype = ctypes.c_size_t
         L.b2x_fp8_gemm.argtypes = [ctypes.POINTER(GemmArgs), ctypes.c_void_p]
         L.b2x_fp8_gemm.restype = ctypes.c_int
+        L.b2x_fp8_gemm_clc.argtypes = [ctypes.POINTER(GemmArgs), ctypes.c_void_p]
+        L.b2x_fp8_gemm_clc.restype = ctypes.c_int
         L.b2x_trace_read.argtypes = [ctypes.c_void_p, ctypes.c_int, ctypes.POINTER(ctypes.c_int)]
         L.b2x_trace_read.restype = ctypes.c_int
         L.b2x_fp8_gemm_swiglu.argtypes = [ctypes.POINTER(GemmArgs), ctypes.c_void_p, ctypes.c_int64, ctypes.c_int,

@@ -301,6 +301,37 @@ def fp8_gemm_fast(a: torch.Tensor, b: torch.Tensor, scale_a: Optional[torch.Tens
     return c
 
 
+def fp8_gemm_clc(a: torch.Tensor, b: torch.Tensor, scale_a: Optional[torch.Tensor], scale_b: Optional[torch.Tensor],
+                 scale_mode: str, out_dtype: torch.dtype, config: Sequence[int]) -> torch.Tensor:
+    """The same GEMM on single-CTA tiles scheduled by cluster launch control
+    (include/b2x.h b2x_fp8_gemm_clc)."""
+    _require_cuda(a, b, scale_a, scale_b)
+    if a.dtype not in FP8_DTYPES or b.dtype not in FP8_DTYPES:
+        raise TypeError(f"fp8_gemm_clc takes float8 A and B, got {a.dtype} and {b.dtype}")
+    if scale_mode not in ("none", "tensor"):
+        raise ValueError("the CLC-scheduled GEMM takes per-tensor scales or none")
+    M, K = a.shape
+    N = b.shape[1]
+    if M == 0 or N == 0:
+        return torch.empty((M, N), dtype=out_dtype, device=a.device)
+    a, b = _tma_friendly(a, b)
+    n8 = -(-N // 8) * 8
+    c = torch.empty((M, n8), dtype=out_dtype, device=a.device)[:, :N]
+    g = _gemm_args(a, b, c, scale_mode, scale_a, scale_b, config)
+    g.config.num_ctas = 1
+    lib = L.lib()
+    with torch.cuda.device(a.device):
+        nws = lib.b2x_gemm_workspace_size(ctypes.byref(g))
+        if nws:
+            ws = _workspace(a.device, nws, zeroed=True)
+            g.workspace, g.workspace_bytes = ws.data_ptr(), ws.numel()
+        st = lib.b2x_fp8_gemm_clc(ctypes.byref(g), ctypes.c_void_p(_stream(a.device)))
+        if st != L.OK:
+            _drop_workspaces()
+        L.check(st)
+    return c
+
+
 @fp8_gemm_op.register_fake
 def _(a, b, scale_a, scale_b, scale_mode, out_dtype, config):
     return a.new_empty((a.shape[0], b.shape[1]), dtype=out_dtype)

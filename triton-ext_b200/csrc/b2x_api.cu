@@ -419,7 +419,7 @@ struct SwArgs {
 // paired kernel with the fused all-reduce epilogue) and b2x_fp8_gemm_swiglu
 // (sw != NULL: the paired kernel with the SwiGLU + quantize epilogue).
 static b2x_status fp8_gemm_impl(const b2x_gemm_args* a, const ArParams* ar, void* stream,
-                                const SwArgs* sw = nullptr) {
+                                const SwArgs* sw = nullptr, bool clc = false) {
   if (!a) return fail(B2X_ERR_INVALID_ARG, "b2x_fp8_gemm: args is NULL");
   if (!is_fp8(a->a_type) || !is_fp8(a->b_type))
     return fail(B2X_ERR_UNSUPPORTED, "b2x_fp8_gemm: A and B must be e4m3 or e5m2 (got %d, %d)", (int)a->a_type,
@@ -486,6 +486,11 @@ static b2x_status fp8_gemm_impl(const b2x_gemm_args* a, const ArParams* ar, void
     c.num_ctas = 2;
     c.block_n = 256;
     c.split_k = 1;
+  }
+  if (clc) {
+    if (blockscaled || mx)
+      return fail(B2X_ERR_UNSUPPORTED, "b2x_fp8_gemm_clc: runs the per-tensor / unscaled GEMM only");
+    c.num_ctas = 1;  // single-CTA tiles: one CTA per unit, scheduled by cluster launch control
   }
   if (mx) {
     if (c.block_n != 128 && c.block_n != 192)
@@ -554,7 +559,8 @@ static b2x_status fp8_gemm_impl(const b2x_gemm_args* a, const ArParams* ar, void
   g.l2_a = 0;
   g.l2_b = 0;
   g.small_m = (!g.pair && !blockscaled && !mx && a->M <= 64) ? 1 : 0;
-  g.swap_ab = (g.small_m && !b_mn && c.block_n == 128) ? 1 : 0;
+  g.swap_ab = (!clc && g.small_m && !b_mn && c.block_n == 128) ? 1 : 0;
+  g.clc = clc ? 1 : 0;
   if (mx) g.ws = reinterpret_cast<float*>(a->workspace);  // tiled scale atoms (fp8_gemm_mx.cu)
   if (c.split_k > 1) {
     g.ws = reinterpret_cast<float*>(a->workspace);
@@ -627,6 +633,11 @@ static b2x_status fp8_gemm_impl(const b2x_gemm_args* a, const ArParams* ar, void
 b2x_status b2x_fp8_gemm(const b2x_gemm_args* a, void* stream) {
   t_err[0] = 0;
   return fp8_gemm_impl(a, nullptr, stream);
+}
+
+b2x_status b2x_fp8_gemm_clc(const b2x_gemm_args* a, void* stream) {
+  t_err[0] = 0;
+  return fp8_gemm_impl(a, nullptr, stream, nullptr, true);
 }
 
 b2x_status b2x_fp8_gemm_swiglu(const b2x_gemm_args* args, void* h, int64_t ld_h, b2x_dtype h_type,

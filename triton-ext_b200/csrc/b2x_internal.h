@@ -66,6 +66,7 @@ struct GemmLaunch {
   int chunk3d;       // small_m with 3-D (x, row, K chunk) A/B tensor maps
   int swap_ab;       // small_m with K-major B: weights on the MMA's M side
   int trace;         // B2X_TRACE=1: per-CTA wait cycles into g_trace
+  int clc;           // cluster-launch-control tile scheduling (single-CTA kernel)
   int l2_a, l2_b;    // L2 eviction policy per operand (0 last, 1 normal, 2 first)
   ArParams ar;       // fused all-reduce (pair kernel only)
   int swiglu;        // fused SwiGLU + fp8 quantize epilogue (pair kernel only)

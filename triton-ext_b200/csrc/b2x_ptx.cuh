@@ -114,6 +114,35 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volati
   }
 }
 
+// ---------------------------------------------------------------- cluster launch control
+// Asks the hardware to cancel one not-yet-launched cluster of this grid; the
+// 16-byte response lands in `resp` (shared, 16-byte aligned) and completes
+// 16 bytes of transaction count on `bar`.  No multicast.
+__device__ __forceinline__ void clc_try_cancel(void* resp, uint64_t* bar) {
+  asm volatile(
+      "clusterlaunchcontrol.try_cancel.async.shared::cta.mbarrier::complete_tx::bytes.b128 [%0], [%1];" ::"r"(
+          smem_u32(resp)),
+      "r"(smem_u32(bar))
+      : "memory");
+}
+
+// x index of the first CTA of the cluster a response cancelled, or -1 when
+// the request found no cluster left to cancel.
+__device__ __forceinline__ int clc_first_ctaid_x(const void* resp) {
+  int x, ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t.reg .b128 r;\n\t"
+      "ld.shared.b128 r, [%2];\n\t"
+      "clusterlaunchcontrol.query_cancel.is_canceled.pred.b128 p, r;\n\t"
+      "selp.u32 %1, 1, 0, p;\n\t"
+      "mov.u32 %0, 0xffffffff;\n\t"
+      "@p clusterlaunchcontrol.query_cancel.get_first_ctaid::x.b32.b128 %0, r;\n\t}"
+      : "=r"(x), "=r"(ok)
+      : "r"(smem_u32(resp))
+      : "memory");
+  return ok ? x : -1;
+}
+
 // ---------------------------------------------------------------- tracing
 // Optional per-CTA cycle counters (enabled per launch by B2X_TRACE=1 on the
 // host; read back with b2x_trace_read).  Slots:

@@ -17,6 +17,18 @@
 // a persistent grid (tile_id += gridDim.x), and a split-K unit covers
 // k_tiles_per_split = cdiv(k_tiles, SPLIT_K) K-blocks (:1258-1264).
 //
+// With p.clc the grid has one CTA per unit and the tiles are handed out by
+// cluster launch control, as in the reference's
+// matmul_kernel_tma_ws_blackwell_clc (extensions/utlx/tlx/tutorials/
+// blackwell_gemm_clc.py:62-281; clc_producer / clc_consumer of
+// tlx/language/tlx/dynamic_launch.py): a CTA starts with the unit of its own
+// index; warp 3 asks the hardware to cancel a CTA that has not launched yet
+// (clusterlaunchcontrol.try_cancel) and publishes the cancelled CTA's index,
+// which is the next unit, through a ring of kClcStages 16-byte responses.
+// The four roles read every response (the epilogue warpgroups included, to
+// keep the tile sequence) and release it; a response with no CTA left ends
+// every role's loop.
+//
 // Thread layout (384 threads): warp 0 producer, warp 1 MMA, warp 2 TMEM
 // allocator, warp 3 spare, warps 4-7 epilogue warpgroup 0, warps 8-11
 // epilogue warpgroup 1.  BLOCK_M = 128 (one tcgen05 M=128 group), BLOCK_K =
@@ -42,6 +54,9 @@ struct MShape {
   static constexpr int kKPS = SMALLM ? (BN == 64 ? 4 : (BN == 128 ? 2 : 1)) : 1;
 };
 
+constexpr int kClcStages = 3;
+constexpr int kClcConsumers = 5;  // producer, MMA, two epilogue warpgroups, the scheduler itself
+
 // SPLITK kernels reduce with red.global and need no C staging tiles.
 template <int BN, int STAGES, int SMALLM = 0, int SPLITK = 0>
 struct SmemLayout {
@@ -57,7 +72,10 @@ struct SmemLayout {
   static constexpr int kBarOff = kCOff + (SPLITK ? 0 : 2 * kCBytes);
   // barriers: full[STAGES], empty[STAGES], tfull[2], tempty[2], mma_done, + tmem slot + flags
   static constexpr int kBarBytes = (2 * STAGES + 5) * 8 + 16;
-  static constexpr int kTotal = kBarOff + kBarBytes;
+  // cluster launch control: kClcStages 16-byte responses, full / empty barriers
+  static constexpr int kClcOff = (kBarOff + kBarBytes + 15) / 16 * 16;
+  static constexpr int kClcBytes = kClcStages * 16 + 2 * kClcStages * 8;
+  static constexpr int kTotal = kClcOff + kClcBytes;
   static constexpr int kAlloc = kTotal + 1024;  // slack to align the base to 1024 B
 };
 
@@ -82,6 +100,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* mma_done = tempty + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(mma_done + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  uint8_t* clc_resp = smem + L::kClcOff;
+  uint64_t* clc_full = reinterpret_cast<uint64_t*>(clc_resp + kClcStages * 16);
+  uint64_t* clc_empty = clc_full + kClcStages;
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -97,9 +118,24 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&tempty[b], 128);
     }
     mbar_init(mma_done, 1);
+    for (int s = 0; s < kClcStages; ++s) {
+      mbar_init(&clc_full[s], 1);
+      mbar_init(&clc_empty[s], kClcConsumers);
+    }
     *abort_flag = 0;
     fence_barrier_init();
   }
+  // Next unit of this CTA with p.clc: the next cluster-launch-control
+  // response (-1: none left); `ci` counts the responses read.  Every reader
+  // waits itself; one thread per role releases the response.
+  auto clc_read = [&](int& ci) -> int {
+    const int s = ci % kClcStages;
+    const uint32_t ph = (uint32_t)(ci / kClcStages) & 1u;
+    ++ci;
+    if (!mbar_wait(&clc_full[s], ph, abort_flag, kStatusTimeoutProducer)) return -1;
+    return clc_first_ctaid_x(clc_resp + s * 16);
+  };
+  auto clc_release = [&](int ci_after) { mbar_arrive(&clc_empty[(ci_after - 1) % kClcStages]); };
   if (warp == 0 && lane == 0) {
     tma_prefetch_desc(&tmA);
     tma_prefetch_desc(&tmB);
@@ -125,7 +161,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       uint32_t issued_mask = 0;
       uint32_t pend_phase[STAGES > 0 ? STAGES : 1];
       bool ok = true;
-      for (int unit = blockIdx.x; unit < p.num_units && ok; unit += gridDim.x) {
+      int ci = 0;
+      for (int unit = blockIdx.x; unit >= 0 && unit < p.num_units && ok;) {
         const int mn = unit % p.num_mn_tiles;
         const int split = unit / p.num_mn_tiles;
         int pid_m, pid_n;
@@ -176,6 +213,12 @@ __global__ void __launch_bounds__(kThreads, 1)
             phase ^= 1;
           }
         }
+        if (p.clc) {
+          unit = clc_read(ci);
+          clc_release(ci);
+        } else {
+          unit += gridDim.x;
+        }
       }
       // Never leave the CTA with TMA writes into its shared memory in flight.
       for (int s = 0; s < STAGES; ++s)
@@ -191,7 +234,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       uint32_t phase = 0;
       int local = 0;
       bool ok = true;
-      for (int unit = blockIdx.x; unit < p.num_units && ok; unit += gridDim.x, ++local) {
+      int ci = 0;
+      for (int unit = blockIdx.x; unit >= 0 && unit < p.num_units && ok; ++local) {
         const int split = unit / p.num_mn_tiles;
         const int k0 = split * p.k_tiles_per_split;
         const int k1 = min(k0 + p.k_tiles_per_split, p.k_tiles);
@@ -232,6 +276,12 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         if (!ok) break;
         mma_commit(&tfull[buf]);
+        if (p.clc) {
+          unit = clc_read(ci);
+          clc_release(ci);
+        } else {
+          unit += gridDim.x;
+        }
       }
       // All MMAs of this thread must finish before TMEM is released.
       mma_commit(mma_done);
@@ -248,9 +298,18 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint8_t* stage_c = smem + L::kCOff + e * L::kCBytes;
     float alpha = 1.0f;
     if (p.scale_mode != B2X_SCALE_NONE) alpha = __fmul_rn(__ldg(p.scale_a), __ldg(p.scale_b));
-    int local = 0;
-    for (int unit = blockIdx.x; unit < p.num_units; unit += gridDim.x, ++local) {
-      if ((local & 1) != e) continue;
+    int local = 0, ci = 0;
+    for (int unit = blockIdx.x; unit >= 0 && unit < p.num_units; ++local) {
+      if ((local & 1) != e) {
+        if (p.clc) {
+          unit = clc_read(ci);
+          named_bar_sync(bar_id, 128);
+          if (wg_tid == 0) clc_release(ci);
+        } else {
+          unit += gridDim.x;
+        }
+        continue;
+      }
       const int mn = unit % p.num_mn_tiles;
       int pid_m, pid_n;
       compute_pid(mn, num_pid_in_group, p.num_pid_m, p.group_size_m, pid_m, pid_n);
@@ -381,8 +440,31 @@ __global__ void __launch_bounds__(kThreads, 1)
           if (wg_tid == 0) p.counters[mn] = 0;
         }
       }
+      if (p.clc) {
+        unit = clc_read(ci);
+        named_bar_sync(bar_id, 128);
+        if (wg_tid == 0) clc_release(ci);
+      } else {
+        unit += gridDim.x;
+      }
     }
     if (!SPLITK && wg_tid == 0) bulk_wait_group0();
+  } else if (warp == 3) {
+    // ------------------------------------------------------------ CLC scheduler
+    if (p.clc && lane == 0) {
+      for (int i = 0;; ++i) {
+        const int s = i % kClcStages;
+        const uint32_t ph = (uint32_t)(i / kClcStages) & 1u;
+        if (!mbar_wait(&clc_empty[s], ph ^ 1u, abort_flag, kStatusTimeoutProducer)) break;
+        fence_proxy_async_smem();  // the consumers' reads of this response precede its rewrite
+        mbar_arrive_expect_tx(&clc_full[s], 16);
+        clc_try_cancel(clc_resp + s * 16, &clc_full[s]);
+        if (!mbar_wait(&clc_full[s], ph, abort_flag, kStatusTimeoutProducer)) break;
+        const int next = clc_first_ctaid_x(clc_resp + s * 16);
+        mbar_arrive(&clc_empty[s]);
+        if (next < 0) break;  // no CTA left: issuing again would be undefined
+      }
+    }
   }
 
   tc_fence_before();
@@ -405,6 +487,7 @@ static cudaError_t launch_gemm_t(const CUtensorMap& ta, const CUtensorMap& tb, c
   constexpr int kS0 = (kMaxDynSmem - (SPLITK ? 0 : 2 * kBM * 128) - 1024 - 256) / kStage;
   constexpr int STAGES = kS0 > 8 ? 8 : kS0;
   using L = SmemLayout<BN, STAGES, SMALLM, SPLITK>;
+  static_assert(L::kAlloc <= 232448, "shared memory layout exceeds the 227 KB per-CTA limit");
   auto kern = fp8_gemm_ws_kernel<BN, STAGES, B_MN, SPLITK, SMALLM>;
   cudaError_t e = ensure_smem_attr(reinterpret_cast<const void*>(kern), L::kAlloc);
   if (e != cudaSuccess) return e;
@@ -456,7 +539,8 @@ cudaError_t launch_fp8_gemm(const GemmLaunch& g, cudaStream_t st) {
   p.ldc = g.ldc;
   p.chunk3d = g.chunk3d;
   p.trace = g.trace;
-  int grid = p.num_units < g.num_sms ? p.num_units : g.num_sms;
+  p.clc = g.clc;
+  int grid = g.clc ? p.num_units : (p.num_units < g.num_sms ? p.num_units : g.num_sms);
   if (g.split_k > 1) {
     return g.b_mn ? dispatch_bn<1, 1>(g.bn, g.small_m, g.tmA, g.tmB, g.tmC, p, grid, st)
                   : dispatch_bn<0, 1>(g.bn, g.small_m, g.tmA, g.tmB, g.tmC, p, grid, st);

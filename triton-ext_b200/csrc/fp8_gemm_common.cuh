@@ -29,6 +29,7 @@ struct GemmParams {
   int64_t ldc;
   int chunk3d;      // small-M kernel: A and B maps are 3-D (x, row, K chunk)
   int trace;        // record per-CTA wait cycles in g_trace
+  int clc;          // single-CTA kernel: tiles handed out by cluster launch control (grid = one CTA per unit)
   int l2_a, l2_b;   // L2 policy per operand: 0 evict_last, 1 evict_normal, 2 evict_first
   ArParams ar;      // fused all-reduce of C over the node's GPUs (paired kernel)
   // fused SwiGLU + fp8 quantize epilogue (paired kernel, fp8_gemm_swiglu.cuh)
