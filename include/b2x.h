@@ -282,6 +282,13 @@ B2X_API b2x_status b2x_fp8_gemm_splitk_noalloc(const b2x_gemm_args* args, void* 
  *                           s = amax / FMAX, written to h_scale [M, I/128]
  *                           (row stride ld_h_scale) -- the A operand scales of
  *                           the block-scaled down projection;
+ *   B2X_SCALE_MX_1x32:      one E8M0 byte per (row, 32 columns of h): the
+ *                           reference's _to_mxfp8_block recipe (mxfp8_utils.py:
+ *                           89-128: amax / FMAX rounded up to a power of two),
+ *                           written to h_scale as uint8 [M, I/32] (row stride
+ *                           ld_h_scale bytes, a multiple of 4; 4-byte aligned
+ *                           base) -- the A operand scales of an MX down
+ *                           projection;
  *   B2X_SCALE_TENSOR_GIVEN: *h_scale supplied by the caller (delayed scaling);
  *                           if h_amax is not NULL, max |h| is max-reduced into
  *                           *h_amax (which the caller zeroes before the call).

@@ -78,6 +78,19 @@ def _run(M, I, K, mode, seed=0):
         assert np.all(np.abs(s - sref) <= 1e-5 * sref + 1e-30), (np.abs(s - sref) / sref).max()
         inv = np.where(s == 0, 0.0, 1.0 / s.astype(np.float64))
         _check_codes(h.view(torch.uint8).cpu().numpy(), href * np.repeat(inv, 128, axis=1))
+    elif mode == "mx1x32":
+        h, s = b2x.gemm_swiglu(X, W, tsx, tsw, mode="mx1x32")
+        torch.cuda.synchronize()
+        s = s.cpu().numpy()
+        # the E8M0 byte of each 32-column group from the oracle's h: it may sit
+        # one step off only where amax / 448 lies within 1e-5 of a power of two
+        gm = np.abs(href).reshape(M, I // 32, 32).max(axis=2) / 448.0
+        want = np.where(gm > 0, np.ceil(np.log2(np.maximum(gm, 1e-300))) + 127, 0).astype(np.int64)
+        diff = s.astype(np.int64) - want
+        near = np.abs(np.log2(np.maximum(gm, 1e-300)) - np.round(np.log2(np.maximum(gm, 1e-300)))) < 1e-5
+        assert np.all((diff == 0) | (near & (np.abs(diff) == 1))), np.abs(diff).max()
+        inv = np.where(s == 0, 0.0, np.exp2(127.0 - s.astype(np.float64)))
+        _check_codes(h.view(torch.uint8).cpu().numpy(), href * np.repeat(inv, 32, axis=1))
     else:
         given = float(np.abs(href).max() / 448.0 * 1.25)
         amax = torch.zeros(1, device="cuda")
@@ -96,6 +109,13 @@ def test_swiglu_block_scales(M, I, K):
     _run(M, I, K, "block1x128")
 
 
+@pytest.mark.parametrize("M,I,K", [(256, 256, 512), (200, 384, 256)])
+def test_swiglu_mx_scales(M, I, K):
+    """The E8M0 1x32 recipe of _to_mxfp8_block (mxfp8_utils.py:89-128) in the
+    epilogue: scale bytes and h codes against the oracle's h."""
+    _run(M, I, K, "mx1x32", seed=2)
+
+
 @pytest.mark.parametrize("M,I,K", [(256, 256, 512), (384, 512, 256)])
 def test_swiglu_given_scale(M, I, K):
     _run(M, I, K, "given", seed=4)
@@ -107,3 +127,29 @@ def test_swiglu_rejects_bad_shapes():
     w = torch.zeros((384, 128), device="cuda", dtype=torch.float8_e4m3fn)  # 2I = 384 is not a multiple of 256
     with pytest.raises(Exception):
         b2x.gemm_swiglu(x, w)
+
+
+def test_swiglu_mx_feeds_mx_down_projection():
+    """gate+up -> SwiGLU -> fp8 h with E8M0 1x32 scales, consumed as-is by the
+    MX (block-scale tensor-core) down GEMM: the chain without a re-quantize
+    pass, checked against the oracle's MX GEMM on the kernel's own h."""
+    import b2x
+    M, I, K, N = 256, 512, 512, 384
+    qx, sx, qg, sg, qu, su = _operands(M, I, K, 7)
+    X = torch.from_numpy(qx).cuda().view(torch.float8_e4m3fn)
+    W = b2x.interleave_gate_up(torch.from_numpy(qg).cuda().view(torch.float8_e4m3fn),
+                               torch.from_numpy(qu).cuda().view(torch.float8_e4m3fn))
+    tsx = torch.tensor([sx], device="cuda")
+    tsw = torch.tensor([sg], device="cuda")  # gate and up share a scale only approximately: fine here
+    h, hs = b2x.gemm_swiglu(X, W, tsx, tsw, mode="mx1x32")
+    g = torch.Generator(device="cuda").manual_seed(3)
+    wd, wds = b2x.quantize(torch.randn((N, I), device="cuda", generator=g), "mx1x32", torch.float8_e4m3fn)
+    out = b2x.matmul(h, wd.t(), {}, scale_a=hs, scale_b=wds)
+    torch.cuda.synchronize()
+    hb, hsb = h.view(torch.uint8).cpu().numpy(), hs.cpu().numpy()
+    wb, wsb = wd.view(torch.uint8).cpu().numpy(), wds.cpu().numpy()
+    ref = O.gemm(hb, wb.T, O.E4M3, O.E4M3, "mx", hsb, wsb)
+    ad = O.fp8_bits_to_f64(hb, O.E4M3) * np.exp2(np.repeat(hsb.astype(np.float64) - 127, 32, axis=1))
+    bd = (O.fp8_bits_to_f64(wb, O.E4M3) * np.exp2(np.repeat(wsb.astype(np.float64) - 127, 32, axis=1))).T
+    err, tol = O.gemm_error(out.float().cpu().numpy(), ref, ad, bd)
+    assert err <= tol, f"{err} > {tol}"

@@ -522,13 +522,14 @@ def gemm_swiglu(x: torch.Tensor, w_gu: torch.Tensor, scale_x: Optional[torch.Ten
     """h = fp8(silu(x . gate^T) * (x . up^T)) for the interleaved weight w_gu
     [2I, K] (interleave_gate_up); see include/b2x.h b2x_fp8_gemm_swiglu.
     mode "block1x128": returns (h [M, I], scales [M, I/128]);
+    mode "mx1x32": returns (h [M, I], E8M0 uint8 scales [M, I/32]) for an MX down projection;
     mode "given": h_scale (one fp32) is used, returns (h, h_scale); if h_amax
     (one fp32, zeroed by the caller) is given, max |h| is accumulated into it."""
     _require_cuda(x, w_gu, scale_x, scale_w, h_scale, h_amax)
     if x.dtype not in FP8_DTYPES or w_gu.dtype not in FP8_DTYPES or h_dtype not in FP8_DTYPES:
         raise TypeError("gemm_swiglu takes float8 operands and produces float8 h")
-    if mode not in ("block1x128", "given"):
-        raise ValueError(f"mode must be 'block1x128' or 'given', got {mode!r}")
+    if mode not in ("block1x128", "mx1x32", "given"):
+        raise ValueError(f"mode must be 'block1x128', 'mx1x32' or 'given', got {mode!r}")
     M, K = x.shape
     N = w_gu.shape[0]
     I = N // 2
@@ -538,6 +539,11 @@ def gemm_swiglu(x: torch.Tensor, w_gu: torch.Tensor, scale_x: Optional[torch.Ten
     if mode == "block1x128":
         sc = torch.empty((M, I // 128 if I % 128 == 0 else I // 128 + 1), dtype=torch.float32, device=x.device)
         ld_sc, smode = sc.stride(0), L.SCALE_BLOCK_1x128
+    elif mode == "mx1x32":
+        if I % 128:
+            raise ValueError("mode 'mx1x32' needs I = N/2 to be a multiple of 128")
+        sc = torch.empty((M, I // 32), dtype=torch.uint8, device=x.device)
+        ld_sc, smode = sc.stride(0), L.SCALE_MX_1x32
     else:
         if h_scale is None:
             raise ValueError("mode 'given' needs h_scale")

@@ -647,8 +647,9 @@ b2x_status b2x_fp8_gemm_swiglu(const b2x_gemm_args* args, void* h, int64_t ld_h,
   if (!args) return fail(B2X_ERR_INVALID_ARG, "b2x_fp8_gemm_swiglu: args is NULL");
   if (h_type != B2X_E4M3 && h_type != B2X_E5M2)
     return fail(B2X_ERR_UNSUPPORTED, "b2x_fp8_gemm_swiglu: h must be e4m3 or e5m2");
-  if (h_mode != B2X_SCALE_BLOCK_1x128 && h_mode != B2X_SCALE_TENSOR_GIVEN)
-    return fail(B2X_ERR_UNSUPPORTED, "b2x_fp8_gemm_swiglu: h scales are BLOCK_1x128 (computed) or TENSOR_GIVEN");
+  if (h_mode != B2X_SCALE_BLOCK_1x128 && h_mode != B2X_SCALE_TENSOR_GIVEN && h_mode != B2X_SCALE_MX_1x32)
+    return fail(B2X_ERR_UNSUPPORTED,
+                "b2x_fp8_gemm_swiglu: h scales are BLOCK_1x128 or MX_1x32 (computed) or TENSOR_GIVEN");
   if (args->scale_mode != B2X_SCALE_NONE && args->scale_mode != B2X_SCALE_TENSOR &&
       args->scale_mode != B2X_SCALE_TENSOR_GIVEN)
     return fail(B2X_ERR_UNSUPPORTED, "b2x_fp8_gemm_swiglu: the gate+up GEMM takes per-tensor scales or none");
@@ -665,11 +666,14 @@ b2x_status b2x_fp8_gemm_swiglu(const b2x_gemm_args* args, void* h, int64_t ld_h,
   if (!h_scale) return fail(B2X_ERR_INVALID_ARG, "b2x_fp8_gemm_swiglu: NULL h_scale");
   if (h_mode == B2X_SCALE_BLOCK_1x128 && ld_h_scale < I / 128)
     return fail(B2X_ERR_INVALID_ARG, "b2x_fp8_gemm_swiglu: ld_h_scale must be >= N/256");
+  if (h_mode == B2X_SCALE_MX_1x32 && (ld_h_scale < I / 32 || (ld_h_scale % 4) || ((uintptr_t)h_scale % 4)))
+    return fail(B2X_ERR_INVALID_ARG,
+                "b2x_fp8_gemm_swiglu: MX scales are uint8 [M, N/64] with a 4-byte aligned base and row stride");
   SwArgs sw;
   sw.h = h;
   sw.ld_h = ld_h;
   sw.fmt = h_type == B2X_E4M3 ? 0 : 1;
-  sw.mode = h_mode == B2X_SCALE_BLOCK_1x128 ? 0 : 1;
+  sw.mode = h_mode == B2X_SCALE_BLOCK_1x128 ? 0 : (h_mode == B2X_SCALE_MX_1x32 ? 2 : 1);
   sw.scale = h_scale;
   sw.ld_scale = ld_h_scale;
   sw.given = h_scale;

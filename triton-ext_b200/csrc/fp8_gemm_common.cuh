@@ -33,9 +33,10 @@ struct GemmParams {
   int l2_a, l2_b;   // L2 policy per operand: 0 evict_last, 1 evict_normal, 2 evict_first
   ArParams ar;      // fused all-reduce of C over the node's GPUs (paired kernel)
   // fused SwiGLU + fp8 quantize epilogue (paired kernel, fp8_gemm_swiglu.cuh)
-  int sw_mode;            // 0: 1x128 block scales written to sw_scale; 1: given scale, amax into sw_amax
+  int sw_mode;            // 0: 1x128 block scales written to sw_scale; 1: given scale, amax into sw_amax;
+                          // 2: MX E8M0 bytes per 32 columns written to sw_scale (uint8, row stride in bytes)
   int sw_fmt;             // 0: e4m3, 1: e5m2
-  float* sw_scale;        // [M, N/256] fp32 (mode 0)
+  float* sw_scale;        // [M, N/256] fp32 (mode 0) or [M, N/64] uint8 (mode 2)
   int64_t sw_ld_scale;
   const float* sw_given;  // mode 1
   float* sw_amax;         // mode 1, optional: max |h| (atomicMax on the bits; start from 0)

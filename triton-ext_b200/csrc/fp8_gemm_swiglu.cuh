@@ -10,6 +10,9 @@
 //   g, u  = alpha * acc[:, 0:128], alpha * acc[:, 128:256]   (alpha = sA * sB)
 //   h     = g / (1 + exp(-g)) * u      (fp32, fast exp and division)
 //   block 1x128 scales:  s = amax_row(|h|) / FMAX, inv = s == 0 ? 0 : 1 / s
+//   MX 1x32 scales:      per 32 columns, d = amax / FMAX rounded up to a power
+//                        of two (RCEIL), E8M0 byte = exponent of d, inv = 1 / d
+//                        (the reference's _to_mxfp8_block, mxfp8_utils.py:89-128)
 //   given scale s:       inv = 1 / s, and amax |h| is max-reduced into *amax
 //   q     = fp8_rne_satfinite(copysign(min(|h * inv|, FMAX), h * inv))
 //
@@ -45,19 +48,37 @@ __device__ __forceinline__ void swiglu_quant_tile(const GemmParams& p, const CUt
                                                   int pid_n, float alpha, uint8_t* stage, uint32_t bar_id, int wg_tid,
                                                   int row, Release release) {
   const float fmax = p.sw_fmt ? 57344.0f : 448.0f;
-  // pass 1: row amax of h
+  // pass 1: row amax of h (and, for MX, the amax of each 32-column group)
   float amax = 0.0f;
+  float gmax[4];
 #pragma unroll 1
   for (int c = 0; c < 128; c += 32) {
     uint32_t g[32], u[32];
     tmem_ld_32x32b_x32(t_row + c, g);
     tmem_ld_32x32b_x32(t_row + 128 + c, u);
     tmem_ld_wait();
+    float m = 0.0f;
 #pragma unroll
-    for (int i = 0; i < 32; ++i) amax = fmaxf(amax, fabsf(swiglu_h(g[i], u[i], alpha)));
+    for (int i = 0; i < 32; ++i) m = fmaxf(m, fabsf(swiglu_h(g[i], u[i], alpha)));
+    gmax[c >> 5] = m;
+    amax = fmaxf(amax, m);
   }
-  float inv;
-  if (p.sw_mode == 0) {
+  float inv = 0.0f;
+  float ginv[4] = {0.f, 0.f, 0.f, 0.f};
+  if (p.sw_mode == 2) {
+    uint32_t bytes = 0;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const float descale = __fdiv_rn(gmax[j], fmax);
+      const uint32_t e = (__float_as_uint(descale) + 0x007FFFFFu) & 0x7F800000u;
+      const float rounded = __uint_as_float(e);
+      ginv[j] = rounded == 0.0f ? 0.0f : __fdiv_rn(1.0f, rounded);
+      bytes |= (e >> 23) << (8 * j);
+    }
+    if (m0 + row < p.M)
+      *reinterpret_cast<uint32_t*>(reinterpret_cast<uint8_t*>(p.sw_scale) + (int64_t)(m0 + row) * p.sw_ld_scale +
+                                   pid_n * 4) = bytes;
+  } else if (p.sw_mode == 0) {
     const float s = __fdiv_rn(amax, fmax);
     inv = s == 0.0f ? 0.0f : __fdiv_rn(1.0f, s);
     if (m0 + row < p.M) p.sw_scale[(int64_t)(m0 + row) * p.sw_ld_scale + pid_n] = s;
@@ -79,13 +100,14 @@ __device__ __forceinline__ void swiglu_quant_tile(const GemmParams& p, const CUt
     tmem_ld_32x32b_x32(t_row + 128 + c, u);
     tmem_ld_wait();
     if (c == 96) release();
+    const float cinv = p.sw_mode == 2 ? ginv[c >> 5] : inv;
     uint32_t w[8];
 #pragma unroll
     for (int j = 0; j < 8; ++j) {
       float y[4];
 #pragma unroll
       for (int k = 0; k < 4; ++k)
-        y[k] = swiglu_clamp(__fmul_rn(swiglu_h(g[4 * j + k], u[4 * j + k], alpha), inv), fmax);
+        y[k] = swiglu_clamp(__fmul_rn(swiglu_h(g[4 * j + k], u[4 * j + k], alpha), cinv), fmax);
       const uint16_t lo = p.sw_fmt ? cvt_e5m2x2(y[0], y[1]) : cvt_e4m3x2(y[0], y[1]);
       const uint16_t hi = p.sw_fmt ? cvt_e5m2x2(y[2], y[3]) : cvt_e4m3x2(y[2], y[3]);
       w[j] = (uint32_t)lo | ((uint32_t)hi << 16);
