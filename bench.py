@@ -459,7 +459,8 @@ def main():
         elif args.workload == "swiglu":
             print(json.dumps(dict(workload="swiglu", shape=[M, N, K], **swiglu_ms(M, N, K, args.steps))))
         elif args.workload == "decode":
-            tf, ms = gemm_tflops(64, 8192, 28672, iters=args.steps, cfg={"SPLIT_K": 8})
+            tf, ms = gemm_tflops(64, 8192, 28672, iters=args.steps,
+                                 cfg={"SPLIT_K": int(os.environ.get("B2X_DECODE_SPLIT_K", "8"))})
             print(json.dumps({"workload": "decode", "tflops": tf, "ms": ms,
                               "gbs": (64 * 28672 + 28672 * 8192 + 64 * 8192 * 2) / (ms * 1e-3) / 1e9}))
         else:
@@ -563,6 +564,9 @@ def main():
         side["decode_splitk8_us"] = round(dms * 1e3, 1)
         side["decode_splitk8_gbs"] = round(dbytes / (dms * 1e-3) / 1e9, 1)
         side["decode_frac_of_hbm"] = round(dbytes / (dms * 1e-3) / 1e9 / peaks["hbm_gbs"], 3)
+        tf, sms_ = gemm_tflops(64, 8192, 28672, cfg={"SPLIT_K": -1})
+        side["decode_streamk_us"] = round(sms_ * 1e3, 1)
+        side["decode_streamk_frac_of_hbm"] = round(dbytes / (sms_ * 1e-3) / 1e9 / peaks["hbm_gbs"], 3)
         tf, _ = gemm_tflops(4096, 7168, 7168, mode="block")
         side["blockscaled_4096x7168x7168_tflops"] = round(tf, 1)
         tf, _ = gemm_tflops(4096, 7168, 7168, mode="mx")
@@ -602,7 +606,7 @@ def main():
                          "frac_of_cublaslt": (gu_flops / (gu * 1e-3) / 1e12 / side["cublaslt_fp8_gate_up_tflops"]
                                               if side.get("cublaslt_fp8_gate_up_tflops") else None),
                          "frac_of_nominal_4500": gu_flops / (gu * 1e-3) / 1e12 / 4500.0,
-                         "traffic": profile_traffic("fp8_gemm_pair_kernel_llama_set.md") if world == 1 else None,
+                         "traffic": profile_traffic("fp8_gemm_pair_kernel_swiglu_gate_up.md") if world == 1 else None,
                          "algorithmic_bytes": (8192 * 8192 + (N // world) * 8192 + 8192 * (N // world) // 2)},
             "e2e": {"value": e2e_val, "unit": "TFLOP/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
             "gpu_launches": launches,

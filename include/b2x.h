@@ -167,7 +167,9 @@ typedef struct {
   int group_size_m;
   int num_smem_buffers, num_tmem_buffers;
   int num_mma_groups, epilogue_subtile;
-  int num_ctas, split_k, interleave_epilogue;
+  int num_ctas, split_k, interleave_epilogue; /* split_k = -1: stream-K for M <= 64 (decode): the K blocks of all
+                                                  tiles are cut into equal ranges, one per SM; partials are reduced
+                                                  like split-K (same workspace) */
   int num_sms; /* NUM_SMS: at most this many SMs for the persistent grid (0 = all); leaves SMs free for concurrent work such as NCCL */
 } b2x_gemm_config;
 

@@ -269,3 +269,24 @@ def test_errors_are_raised_not_faulted():
         b2x.matmul(A, rowmajor_b, {}, scale_a=torch.ones((128, 1), device="cuda"),
                    scale_b=torch.ones((1, 1), device="cuda"))
     assert b2x.read_device_status() == 0
+
+
+@pytest.mark.parametrize("M,N,K", [(64, 8192, 28672), (16, 1000, 3000), (33, 4096, 7168), (1, 256, 128)])
+def test_stream_k_decode(M, N, K):
+    """SPLIT_K = -1 (stream-K): K blocks of all tiles cut into one equal range
+    per SM, so ranges cross tile boundaries and a tile is summed from a
+    varying number of pieces.  Against the oracle (sampled columns for the
+    decode benchmark shape) and against non-split, three calls in a row (the
+    workspace and the tile counters must come back clean)."""
+    a, sa = _quant((M, K), O.E4M3, 40 + M)
+    b, sb = _quant((K, N), O.E4M3, 41)
+    c1 = _gemm(a, b, O.E4M3, O.E4M3, sa, sb, "kmajor", config={"SPLIT_K": 1})
+    cols = np.random.default_rng(1).choice(N, min(N, 512), replace=False)
+    ad = O.fp8_bits_to_f64(a, O.E4M3) * sa
+    bd = O.fp8_bits_to_f64(b[:, cols], O.E4M3) * sb
+    ref = ad @ bd
+    for rep in range(3):
+        c = _gemm(a, b, O.E4M3, O.E4M3, sa, sb, "kmajor", config={"SPLIT_K": -1})
+        _check(c[:, cols], ref, ad, bd, f"stream-K {M}x{N}x{K} rep={rep}")
+        _check(c, c1.astype(np.float64), ad, O.fp8_bits_to_f64(b, O.E4M3) * sb, "stream-K vs non-split")
+    assert _b2x().read_device_status() == 0

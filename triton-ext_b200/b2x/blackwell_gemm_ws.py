@@ -274,6 +274,9 @@ def _to_b2x_config(cfg: dict, K: int) -> list:
     if bn and bn not in (64, 128, 192, 256):
         bn = min((64, 128, 256), key=lambda v: abs(v - bn))
     group = int(cfg.get("GROUP_SIZE_M", 0)) * max(1, bm // 128)
+    if cfg.get("STREAM_K") or int(cfg.get("SPLIT_K", 1)) == -1:
+        # stream-K (decode, M <= 64): K blocks spread evenly over the SMs
+        return [128, 128, 128, int(cfg.get("GROUP_SIZE_M", 0)), 0, 2, 1, 1, 1, -1, 0, int(cfg.get("NUM_SMS", 0))]
     sk = max(1, int(cfg.get("SPLIT_K", 1)))
     k_tiles = -(-K // 128)
     while sk > 1 and (k_tiles < sk or (sk - 1) * -(-k_tiles // sk) >= k_tiles):

@@ -399,7 +399,7 @@ size_t b2x_gemm_workspace_size(const b2x_gemm_args* a) {
   if (b2x_gemm_default_config(a, &c) != B2X_OK) return 0;
   if (a->scale_mode == B2X_SCALE_MX_1x32 && a->M > 0 && a->N > 0 && a->K > 0)
     return mx_workspace_bytes(a->M, a->N, a->K, c.block_n);
-  if (c.split_k <= 1) return 0;
+  if (c.split_k == 1 || c.split_k == 0) return 0;  // > 1: split-K; -1: stream-K (small M)
   uint64_t tiles = (uint64_t)ceil_div(a->M, 128) * ceil_div(a->N, c.block_n);
   return (size_t)(align_up((uint64_t)a->M * a->N * 4, 256) + align_up(tiles * 4, 256));
 }
@@ -508,7 +508,19 @@ static b2x_status fp8_gemm_impl(const b2x_gemm_args* a, const ArParams* ar, void
     return fail(B2X_ERR_UNSUPPORTED,
                 "b2x_fp8_gemm: block-scaled GEMM runs with SPLIT_K = 1 and 128-wide tiles (256 on CTA pairs)");
   const int k_tiles = ceil_div(a->K, 128);
-  if (c.split_k < 1) return fail(B2X_ERR_INVALID_ARG, "b2x_fp8_gemm: SPLIT_K must be >= 1");
+  const bool stream_k = c.split_k == -1;
+  if (stream_k && !(a->M <= 64 && !b_mn && !blockscaled && !mx && !ar && !sw && !clc && c.block_n == 128))
+    return fail(B2X_ERR_UNSUPPORTED,
+                "b2x_fp8_gemm: SPLIT_K = -1 (stream-K) is built for the small-M kernel: M <= 64, a K-major B, "
+                "per-tensor scales, 128-wide tiles");
+  if (c.split_k < 1 && !stream_k) return fail(B2X_ERR_INVALID_ARG, "b2x_fp8_gemm: SPLIT_K must be >= 1 (or -1)");
+  if (stream_k) {
+    if (a->N % 4) return fail(B2X_ERR_UNSUPPORTED, "b2x_fp8_gemm: stream-K needs N %% 4 == 0");
+    size_t need = b2x_gemm_workspace_size(a);
+    if (!a->workspace || a->workspace_bytes < need || ((uintptr_t)a->workspace % 16))
+      return fail(B2X_ERR_WORKSPACE, "b2x_fp8_gemm: stream-K needs a zeroed %zu-byte workspace (got %zu)", need,
+                  a->workspace_bytes);
+  }
   if (c.split_k > 1) {
     int kps = ceil_div(k_tiles, c.split_k);
     if ((int64_t)(c.split_k - 1) * kps >= k_tiles)
@@ -562,7 +574,7 @@ static b2x_status fp8_gemm_impl(const b2x_gemm_args* a, const ArParams* ar, void
   g.swap_ab = (!clc && g.small_m && !b_mn && c.block_n == 128) ? 1 : 0;
   g.clc = clc ? 1 : 0;
   if (mx) g.ws = reinterpret_cast<float*>(a->workspace);  // tiled scale atoms (fp8_gemm_mx.cu)
-  if (c.split_k > 1) {
+  if (c.split_k > 1 || stream_k) {
     g.ws = reinterpret_cast<float*>(a->workspace);
     g.counters = reinterpret_cast<int*>(reinterpret_cast<uint8_t*>(a->workspace) +
                                         align_up((uint64_t)a->M * a->N * 4, 256));

@@ -131,7 +131,8 @@ __device__ __forceinline__ void ar_reduce_unit(const GemmParams& p, int unit, in
       }
     }
   }
-  fence_acq_rel_sys();  // this thread's share of the sum is visible on every rank
+  // No per-thread fence: the caller orders every thread's stores before the
+  // done signal with a warpgroup barrier and one system-scope fence.
 }
 
 // Ring of owned units in shared memory, from the two epilogue warpgroups
@@ -222,6 +223,10 @@ __device__ __forceinline__ bool ar_reducer(const GemmParams& p, int n_owned, int
     ar_reduce_unit<AR>(p, cmd, wg_tid);
     named_bar_sync(bar_id, 128);
     if (wg_tid == 0) {
+      // The barrier above orders the warpgroup's stores of the sum before this
+      // thread's fence; the fence (cumulative) makes them visible on every
+      // rank before the done signal.
+      fence_acq_rel_sys();
       trace_add(p.trace, 8, (unsigned long long)(clock64() - t0));
       trace_add(p.trace, 10, 1);
       if constexpr (AR == 1) {

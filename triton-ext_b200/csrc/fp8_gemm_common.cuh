@@ -29,6 +29,7 @@ struct GemmParams {
   int64_t ldc;
   int chunk3d;      // small-M kernel: A and B maps are 3-D (x, row, K chunk)
   int trace;        // record per-CTA wait cycles in g_trace
+  int stream_k;     // small-M kernel: K blocks of all tiles spread evenly over the grid (SPLIT_K = -1)
   int clc;          // single-CTA kernel: tiles handed out by cluster launch control (grid = one CTA per unit)
   int l2_a, l2_b;   // L2 policy per operand: 0 evict_last, 1 evict_normal, 2 evict_first
   ArParams ar;      // fused all-reduce of C over the node's GPUs (paired kernel)

@@ -12,6 +12,14 @@
 // one token row) and the last unit of a tile converts and re-zeroes it, as in
 // the main kernel.  Tile order and K ranges follow the reference's split-K
 // scheme (blackwell_gemm_ws.py:1258-1264).
+//
+// Stream-K (p.stream_k, SPLIT_K = -1): the K blocks of all tiles, taken as one
+// flat sequence (tile-major), are cut into gridDim.x equal ranges, one per
+// CTA, so every SM streams the same number of weight bytes whatever the tile
+// count (a fixed split leaves the last wave partly empty: 64 tiles x 8 splits
+// is 3.46 waves on 148 SMs).  A CTA's range crosses one or more tiles; each
+// piece is a segment, reduced like a split-K unit, and a tile is finished by
+// the last of the CTAs whose ranges touch it.
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
 #include <cstdint>
@@ -39,6 +47,36 @@ struct SmLayout {
   static constexpr int kBarBytes = (2 * kStages + 5) * 8 + 16;
   static constexpr int kAlloc = kBarOff + kBarBytes + 1024;
 };
+
+// Segment i of this CTA: tile nt, K blocks [k0, k1), and the number of
+// segments (over all CTAs) that cover the tile.  False past the last one.
+struct SmSeg {
+  int nt, k0, k1, parts;
+};
+__device__ __forceinline__ bool smallm_segment(const GemmParams& p, int i, SmSeg& sg) {
+  if (!p.stream_k) {
+    const int unit = blockIdx.x + i * gridDim.x;
+    if (unit >= p.num_units) return false;
+    sg.nt = unit % p.num_mn_tiles;
+    const int split = unit / p.num_mn_tiles;
+    sg.k0 = split * p.k_tiles_per_split;
+    sg.k1 = min(sg.k0 + p.k_tiles_per_split, p.k_tiles);
+    sg.parts = p.split_k;
+    return true;
+  }
+  const int64_t KT = p.k_tiles;
+  const int64_t total = (int64_t)p.num_mn_tiles * KT;
+  const int64_t W = (total + gridDim.x - 1) / gridDim.x;
+  const int64_t lo = (int64_t)blockIdx.x * W, hi = min(total, lo + W);
+  if (lo >= hi) return false;
+  const int64_t t = lo / KT + i;
+  if (t * KT >= hi) return false;
+  sg.nt = (int)t;
+  sg.k0 = (int)(max(lo, t * KT) - t * KT);
+  sg.k1 = (int)(min(hi, (t + 1) * KT) - t * KT);
+  sg.parts = (int)(((t + 1) * KT - 1) / W - (t * KT) / W + 1);
+  return true;
+}
 
 // tmW: weights [N, K] K-major, box {128, 128}; tmA: activations [M, K], box {128, NT}.
 template <int NT, int SPLITK>
@@ -96,11 +134,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       uint32_t phase = 0, issued_mask = 0;
       uint32_t pend_phase[S];
       bool ok = true;
-      for (int unit = blockIdx.x; unit < p.num_units && ok; unit += gridDim.x) {
-        const int nt = unit % p.num_mn_tiles;
-        const int split = unit / p.num_mn_tiles;
-        const int k0 = split * p.k_tiles_per_split;
-        const int k1 = min(k0 + p.k_tiles_per_split, p.k_tiles);
+      SmSeg sg;
+      for (int si = 0; ok && smallm_segment(p, si, sg); ++si) {
+        const int nt = sg.nt, k0 = sg.k0, k1 = sg.k1;
         for (int kb = k0; kb < k1; kb += kSmKPS) {
           if (!mbar_wait_traced(&empty[stage], phase ^ 1, abort_flag, kStatusTimeoutProducer, p.trace, 0)) {
             ok = false;
@@ -134,10 +170,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       uint32_t phase = 0;
       int local = 0;
       bool ok = true;
-      for (int unit = blockIdx.x; unit < p.num_units && ok; unit += gridDim.x, ++local) {
-        const int split = unit / p.num_mn_tiles;
-        const int k0 = split * p.k_tiles_per_split;
-        const int k1 = min(k0 + p.k_tiles_per_split, p.k_tiles);
+      SmSeg sg;
+      for (int si = 0; ok && smallm_segment(p, si, sg); ++si, ++local) {
+        const int k0 = sg.k0, k1 = sg.k1;
         const int buf = local & 1;
         const uint32_t use = (uint32_t)(local >> 1);
         trace_add(p.trace, 7, 1);
@@ -185,9 +220,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (p.scale_mode != B2X_SCALE_NONE) alpha = __fmul_rn(__ldg(p.scale_a), __ldg(p.scale_b));
     __shared__ int s_last[2];
     int local = 0;
-    for (int unit = blockIdx.x; unit < p.num_units; unit += gridDim.x, ++local) {
+    SmSeg sg;
+    for (int si = 0; smallm_segment(p, si, sg); ++si, ++local) {
       if ((local & 1) != e) continue;
-      const int nt = unit % p.num_mn_tiles;
+      const int nt = sg.nt;
       const uint32_t use = (uint32_t)(local >> 1);
       bool ok = mbar_wait_traced(&tfull[e], use & 1, abort_flag, kStatusTimeoutEpilogue, p.trace && wg_tid == 0,
                                  3 + e);
@@ -234,7 +270,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         named_bar_sync(bar_id, 128);
         if (wg_tid == 0) {
           int old = atomic_add_acq_rel_gpu(p.counters + nt, 1);
-          s_last[e] = (old == p.split_k - 1);
+          s_last[e] = (old == sg.parts - 1);
         }
         named_bar_sync(bar_id, 128);
         if (s_last[e]) {
@@ -310,9 +346,17 @@ cudaError_t launch_fp8_gemm_smallm(const GemmLaunch& g, cudaStream_t st) {
   p.c = g.c;
   p.ldc = g.ldc;
   p.trace = g.trace;
-  const int grid = p.num_units < g.num_sms ? p.num_units : g.num_sms;
+  p.stream_k = g.split_k < 0;
+  if (p.stream_k) {  // one flat K-block sequence over all tiles, cut into grid equal ranges
+    p.split_k = 2;   // any value > 1: selects the reducing epilogue
+    p.num_units = p.num_mn_tiles;
+    p.k_tiles_per_split = p.k_tiles;
+  }
+  const int64_t items = (int64_t)p.num_mn_tiles * p.k_tiles;
+  const int grid = p.stream_k ? (int)(items < g.num_sms ? items : g.num_sms)
+                              : (p.num_units < g.num_sms ? p.num_units : g.num_sms);
   // g.tmB holds the weights (box {128, 128}), g.tmA the activations (box {128, NT}).
-  if (g.split_k > 1) {
+  if (g.split_k > 1 || p.stream_k) {
     switch (NT) {
       case 16: return launch_smallm_t<16, 1>(g.tmB, g.tmA, p, grid, st);
       case 32: return launch_smallm_t<32, 1>(g.tmB, g.tmA, p, grid, st);
